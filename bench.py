@@ -1,0 +1,366 @@
+"""Benchmark of the fused spectral-eviction decode kernel (B200).
+
+Workload (BASELINE config 2 at its headline size): V2 multi-head decode,
+32 heads, head_dim 128, 32K tokens, fp16, the 50/50 smooth/noisy tile
+mixture, ζ_max = 1.0 (≈50 % eviction).  One step = one decode call over one
+batch of synthetic input.  ``value`` = algorithmic bytes (all K read once +
+V of the retained tiles + q + out) per second over the timed steps, summed
+over ranks; ``e2e`` = the same metric through the public API with host
+(pinned) inputs copied to the device and the output copied back every step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs one process per GPU (torchrun); every rank decodes its own
+sequence batch (heads / batch sharding, no collective on the data path) and
+the timed region is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HEADS, HEAD_DIM, SEQ, DTYPE, ZETA = 32, 128, 32768, torch.float16, 1.0
+L2_BYTES = 126 * 2 ** 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seq", type=int, default=SEQ)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-sample-heads", type=int, default=0, help="0 = auto (about 10-30 s of CPU work)")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """DRAM bytes per launch from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "v2_fp16_h32_s32k_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.lines, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(seq, seed, device):
+    from orthocache_gpu_b200.synthetic import mha_inputs_device
+    return None, mha_inputs_device(HEADS, seq, HEAD_DIM, seed=seed, device=device, dtype=DTYPE)
+
+
+def algorithmic_bytes(num_tiles_total, retained, esz=2, hd=HEAD_DIM, heads=HEADS):
+    return (num_tiles_total * 64 * hd * esz + retained * 64 * hd * esz + 2 * heads * hd * esz)
+
+
+def dense_decode_us(q, k, v, reps=50):
+    """Dense flash-decoding on the same inputs (flashinfer if usable, else torch SDPA)."""
+    res = {}
+    try:
+        import flashinfer
+        fn = lambda: flashinfer.single_decode_with_kv_cache(q, k, v, kv_layout="HND")  # noqa: E731
+        fn()
+        res["flashinfer_us"] = time_fn(fn, reps)
+    except Exception as e:  # noqa: BLE001
+        res["flashinfer_error"] = type(e).__name__
+    try:
+        qq, kk, vv = q[None, :, None, :], k[None], v[None]
+        fn = lambda: torch.nn.functional.scaled_dot_product_attention(qq, kk, vv)  # noqa: E731
+        fn()
+        res["torch_sdpa_us"] = time_fn(fn, reps)
+    except Exception as e:  # noqa: BLE001
+        res["torch_sdpa_error"] = type(e).__name__
+    return res
+
+
+def time_fn(fn, reps):
+    for _ in range(3):
+        fn()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) * 1000.0 / reps
+
+
+def graph_of(fn, n):
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()  # warm (workspace allocation happens outside capture)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(n):
+                fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    return g
+
+
+def cpu_baseline(seq, sample_heads=8, min_seconds=10.0):
+    """Oracle (NumPy restatement of the reference CPU path) on a bounded sample.
+
+    The sample is ``sample_heads`` heads of the workload (same shape, seeded
+    mixture), decoded repeatedly until ``min_seconds`` of CPU work is timed.
+    """
+    from oracle import orthocache_oracle as orc
+    from orthocache_gpu_b200.synthetic import mha_inputs
+    x = mha_inputs(sample_heads, seq, HEAD_DIM, seed=0)
+    q, k, v = (torch.from_numpy(a).to(DTYPE).float().numpy() for a in (x.q, x.keys, x.values))
+    reps, nb = 0, 0
+    t0 = time.perf_counter()
+    while True:
+        _, meta = orc.v2_attention(q, k, v, ZETA)
+        reps += 1
+        nb += algorithmic_bytes(sample_heads * (seq // 64), meta["tiles_retained"], heads=sample_heads)
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            break
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count()
+    return {"value": nb / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{sample_heads} of {HEADS} heads x {seq} tokens (same mixture), oracle NumPy "
+                      f"float32/64, {reps} passes in {dt:.1f} s"}
+
+
+def main():
+    a = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = world > 1
+    if a.impl == "reference" and dist and rank != 0:
+        return
+    if dist:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    seq = a.seq
+    ntiles = HEADS * (seq // 64)
+    config = {"workload": f"V2 split-K decode, {HEADS} heads x {seq} tokens, head_dim {HEAD_DIM}, fp16, "
+                          f"tile mixture 50/50, zeta_max {ZETA} (50% evict)",
+              "heads": HEADS, "seq_len": seq, "head_dim": HEAD_DIM, "zeta_max": ZETA,
+              "l2": "inputs larger than L2 (two input sets alternate, 0.54 GB each)",
+              "parallelism": f"heads/batch sharded x{world} (independent sequences per rank)"}
+    metric = "decode attention achieved HBM GB/s (algorithmic bytes: all K + retained V), 32K ctx, 50% evict"
+
+    if a.impl == "reference":
+        sh = a.cpu_sample_heads or 8
+        nsteps = max(1, min(a.steps, 5))
+        cpu_baseline(seq, sh, min_seconds=0.0)         # warm-up pass
+        vals = [cpu_baseline(seq, sh, min_seconds=10.0) for _ in range(nsteps)]
+        v = statistics.median(r["value"] for r in vals)
+        line = {"impl": "reference", "metric": metric, "value": v, "unit": "GB/s", "n_gpus": a.gpus,
+                "steps": len(vals), "warmup": 1, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+                "cpu_baseline": {**vals[0], "value": v},
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import orthocache_gpu_b200 as oc
+    from orthocache_gpu_b200 import _lib
+
+    _, (q, k, v) = make_inputs(seq, rank, dev)
+    _, (q2, k2, v2) = make_inputs(seq, rank + 1000, dev)
+    sets = [(q, k, v), (q2, k2, v2)]
+
+    # retained tiles (deterministic per input set) for the byte count
+    kept = []
+    for (qq, kk, vv) in sets:
+        _, meta = oc.fused_orthocache_attention_v2(qq, kk, vv, ZETA)
+        kept.append(meta["tiles_retained"])
+    nsplit = oc.fused_orthocache_attention_v2(q, k, v, ZETA, stats=False)[1]["num_splits"]
+    bytes_per = [algorithmic_bytes(ntiles, r) for r in kept]
+
+    def step(i=0):
+        qq, kk, vv = sets[i % 2]
+        oc.fused_orthocache_attention_v2(qq, kk, vv, ZETA, stats=False)
+
+    chunk = min(a.steps, 500)
+    graphs = graph_of(step, chunk)
+    for _ in range(max(3, a.warmup // chunk + 1)):
+        graphs.replay()
+    reps = max(1, a.steps // chunk)
+    steps = reps * chunk
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(reps):
+            graphs.replay()
+        e.record()
+        torch.cuda.synchronize()
+        if clk.proc:
+            time.sleep(0.25)
+    if dist:
+        torch.distributed.barrier()
+    ms = s.elapsed_time(e)
+    t = torch.tensor([ms], device=dev)
+    if dist:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(t.item())
+    per_step_bytes = sum(bytes_per[i % 2] for i in range(steps)) / steps
+    value = per_step_bytes * steps * world / (ms_max / 1e3) / 1e9
+    launch_us = ms / steps * 1000.0
+    achieved = per_step_bytes / (launch_us * 1e-6) / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # e2e: public API, pinned host inputs -> device -> kernel -> host output
+    hq, hk, hv = (t_.cpu().pin_memory() for t_ in (q, k, v))
+    h2d = hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2
+    d2h = HEADS * HEAD_DIM * 2
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        out, _ = oc.fused_orthocache_attention_v2(dq, dk, dv, ZETA, stats=False)
+        return out.cpu()
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record()
+    for _ in range(a.e2e_steps):
+        e2e_step()
+    ee.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([es.elapsed_time(ee)], device=dev)
+    if dist:
+        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+    e2e_value = bytes_per[0] * a.e2e_steps * world / (float(te.item()) / 1e3) / 1e9
+
+    extra = {}
+    if rank == 0 and not a.no_sweep:
+        sweep = []
+        for sl in (1024, 2048, 4096, 8192, 16384, 32768):
+            if sl == seq:
+                qs, ks, vs, kp = q, k, v, kept[0]
+            else:
+                _, (qs, ks, vs) = make_inputs(sl, 7, dev)
+                kp = oc.fused_orthocache_attention_v2(qs, ks, vs, ZETA)[1]["tiles_retained"]
+            us = time_fn(lambda: oc.fused_orthocache_attention_v2(qs, ks, vs, ZETA, stats=False), 200)
+            g1 = graph_of(lambda i=0: oc.fused_orthocache_attention_v2(qs, ks, vs, ZETA, stats=False), 50)
+            gus = time_fn(g1.replay, 10) / 50
+            nb = algorithmic_bytes(HEADS * (sl // 64), kp)
+            row = {"seq_len": sl, "us_eager": round(us, 2), "us_graph": round(gus, 2),
+                   "gbs": round(nb / (gus * 1e-6) / 1e9, 1), "evict": round(1 - kp / (HEADS * sl // 64), 3)}
+            row.update({kk_: round(vv_, 2) if isinstance(vv_, float) else vv_
+                        for kk_, vv_ in dense_decode_us(qs, ks, vs).items()})
+            sweep.append(row)
+            if sl != seq:
+                del qs, ks, vs
+        extra["sweep"] = sweep
+
+    if rank == 0:
+        cb = cpu_baseline(seq, a.cpu_sample_heads or 8)
+        tr = committed_traffic()
+        line = {
+            "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": max(3, a.warmup), "ms_per_step": round(ms_max / steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {**config, "num_splits": nsplit, "evict_rate": round(1 - kept[0] / ntiles, 4)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "frac_of_8tbs": round(achieved / 8000.0, 4),
+                         "traffic": tr["dram_bytes_per_launch"] if tr else None,
+                         "algorithmic_bytes": int(bytes_per[0]),
+                         "launch_us": round(launch_us, 3)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cb,
+            **extra,
+        }
+        print(json.dumps(line))
+    if dist:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

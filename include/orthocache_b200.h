@@ -1,0 +1,169 @@
+/*
+ * orthocache_b200.h - C ABI of the B200 (sm_100a) fused spectral-eviction
+ * decode-attention library (liborthocache_b200.so).
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * launches on the given CUDA stream (a cudaStream_t passed as void*; NULL is
+ * the legacy default stream), never allocates memory and never synchronises.
+ * Returns OC_OK or an OC_ERR_* code; oc_status_string() names a code.
+ *
+ * Reference interfaces replaced (paths are in j-arndt/orthocache-gpu,
+ * src/orthocache_gpu/triton_kernels/):
+ *   oc_fwht_eviction          fwht_fused_prototype.py:255-322  triton_fwht_eviction
+ *   oc_fused_attention_v1     fused_eviction.py:698-800        fused_orthocache_attention
+ *   oc_fused_attention_v2     fused_eviction.py:573-691        fused_orthocache_attention_v2
+ *   oc_fused_attention_v3_gqa gqa_eviction.py:511-639          fused_orthocache_attention_v3_gqa
+ *   oc_fused_attention_paged  paged_eviction.py:323-445        fused_orthocache_attention_paged
+ *   oc_lse_merge              fused_eviction.py:316-373        _splitk_reduce_kernel (as a
+ *                             stand-alone merge of split partials, used across GPUs)
+ *
+ * Dtype codes: OC_F32, OC_F16, OC_BF16 for queries, values and outputs;
+ * keys may also be OC_F8E4M3 (k_scale is folded into q by the caller, as the
+ * reference does).  K and V must have the same dtype unless K is OC_F8E4M3.
+ * head_dim: 16, 32, 64, 128 or 256 (float32 keys: up to 128).  Tile size 64.
+ * Base pointers and token / head / block strides must be multiples of 16
+ * bytes (the tiles are moved by the bulk-copy engine).
+ *
+ * Thresholds are given in double precision and compared exactly as the
+ * reference's CPU path compares them (see the notes at each function).
+ *
+ * Workspace: split-K partials and merge tickets.  Size it with
+ * oc_workspace_bytes(); it must be zero-filled once before first use and is
+ * left zeroed by every successful launch.  Launches that share a workspace
+ * must not overlap on the GPU.  A non-zero *status word after a launch
+ * (OC_STATUS_*) means the outputs of that launch are invalid; re-zero the
+ * workspace before reusing it.
+ */
+#ifndef ORTHOCACHE_B200_H
+#define ORTHOCACHE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { OC_F32 = 0, OC_F16 = 1, OC_BF16 = 2, OC_F8E4M3 = 3 };
+
+enum {
+  OC_OK = 0,
+  OC_ERR_INVALID = 1,     /* bad pointer, size, stride or alignment */
+  OC_ERR_UNSUPPORTED = 2, /* dtype / head_dim combination not compiled */
+  OC_ERR_WORKSPACE = 3,   /* workspace too small */
+  OC_ERR_CUDA = 4         /* the launch failed; see cudaGetLastError */
+};
+
+/* bits of the device status word */
+enum { OC_STATUS_TIMEOUT = 1, OC_STATUS_BAD_PAGE = 2, OC_STATUS_BAD_SEQLEN = 4 };
+
+/* gate selector of oc_fused_attention_paged */
+enum { OC_GATE_ZETA = 0, OC_GATE_CAUCHY_SCHWARZ = 2 };
+
+const char* oc_status_string(int code);
+
+/* Library version, e.g. 100 for 0.1.0. */
+int oc_version(void);
+
+/* Bytes of workspace for a launch over `num_groups` (sequence, kv-head)
+ * pairs with `group` query heads each, `num_splits` splits and `head_dim`.
+ * Zero when num_splits == 1. */
+size_t oc_workspace_bytes(int64_t num_groups, int group, int num_splits, int head_dim);
+
+/* The reference's split heuristic: min(num_sms, max(1, num_tiles/4), num_tiles),
+ * at least 1 (fused_eviction.py:556-570). */
+int oc_auto_num_splits(int64_t num_tiles, int num_sms);
+
+/* ζ mask for one head: keys (num_tokens, head_dim), token stride in elements.
+ * mask_out[t] = (ζ_t <= float32(zeta_max)) as 0/1 bytes (fwht_fused_prototype.py:246;
+ * a NaN ζ is evicted); zeta_out (nullable) receives ζ_t as float32. */
+int oc_fwht_eviction(const void* keys, int k_dtype, int64_t num_tokens, int head_dim,
+                     int64_t k_tok_stride, double zeta_max, uint8_t* mask_out, float* zeta_out,
+                     uint32_t* status, void* stream);
+
+/* Multi-head ζ-gated decode (V2).  q (num_heads, head_dim); keys / values
+ * (num_heads, seq_len, head_dim) with the given element strides; out
+ * (num_heads, head_dim) with out_head_stride.  A tile is evicted iff
+ * ζ > zeta_max in double precision (fused_eviction.py:428-432), so a NaN ζ
+ * is retained.  mask_out (nullable): (num_heads, seq_len/64) retain flags.
+ * retained (nullable): += number of retained tiles.  num_splits <= 0 selects
+ * oc_auto_num_splits(num_tiles, num_sms). */
+int oc_fused_attention_v2(const void* q, int q_dtype, int64_t q_head_stride,
+                          const void* keys, int k_dtype, int64_t k_head_stride, int64_t k_tok_stride,
+                          const void* values, int v_dtype, int64_t v_head_stride, int64_t v_tok_stride,
+                          int num_heads, int64_t seq_len, int head_dim, double zeta_max,
+                          int num_splits, int num_sms, void* out, int out_dtype, int64_t out_head_stride,
+                          uint8_t* mask_out, uint32_t* retained, uint32_t* status,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Single-head ζ-gated decode (V1): oc_fused_attention_v2 with num_heads = 1;
+ * q (1, head_dim), keys / values (seq_len, head_dim). */
+int oc_fused_attention_v1(const void* q, int q_dtype, const void* keys, int k_dtype, int64_t k_tok_stride,
+                          const void* values, int v_dtype, int64_t v_tok_stride, int64_t seq_len,
+                          int head_dim, double zeta_max, int num_sms, void* out, int out_dtype,
+                          uint8_t* mask_out, uint32_t* retained, uint32_t* status, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* GQA decode with the Cauchy-Schwarz gate (V3), with an optional leading
+ * batch of `num_seqs` independent sequences (num_seqs = 1 is the reference's
+ * layout).  q (num_seqs, num_kv_heads*group, head_dim); keys / values
+ * (num_seqs, num_kv_heads, seq_len, head_dim); out like q.  Query heads
+ * [h*group, (h+1)*group) share kv head h.  A tile is evicted iff
+ * max_g(|q_g| * |K_high|_F) <= tau in double precision, norms below 1e-38
+ * read as 0 (gqa_eviction.py:216-239). */
+int oc_fused_attention_v3_gqa(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                              const void* keys, int k_dtype, int64_t k_seq_stride, int64_t k_head_stride,
+                              int64_t k_tok_stride, const void* values, int v_dtype, int64_t v_seq_stride,
+                              int64_t v_head_stride, int64_t v_tok_stride, int num_seqs, int num_kv_heads,
+                              int group, int64_t seq_len, int head_dim, double tau, int num_splits,
+                              int num_sms, void* out, int out_dtype, int64_t out_seq_stride,
+                              int64_t out_head_stride, uint8_t* mask_out, uint32_t* retained,
+                              uint32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Paged-KV decode.  q (num_seqs, num_kv_heads*group, head_dim); caches
+ * (num_blocks, num_kv_heads, block_size, head_dim) addressed through element
+ * strides; block_tables (num_seqs, max_blocks) int32 with row stride
+ * bt_seq_stride.  seq_lens (nullable, int32, multiples of 64): tokens of each
+ * sequence; NULL means max_blocks*block_size for every sequence, the
+ * reference's behaviour.  gate = OC_GATE_ZETA (threshold = zeta_max, the
+ * reference's paged path) or OC_GATE_CAUCHY_SCHWARZ (threshold = tau).
+ * block_size: power of two.  group = 1 with OC_GATE_ZETA is exactly the
+ * reference's MHA paged kernel. */
+int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                             const void* k_cache, int k_dtype, int64_t k_blk_stride, int64_t k_head_stride,
+                             int64_t k_tok_stride, const void* v_cache, int v_dtype, int64_t v_blk_stride,
+                             int64_t v_head_stride, int64_t v_tok_stride, int num_blocks, int block_size,
+                             const int32_t* block_tables, int64_t bt_seq_stride, int max_blocks,
+                             const int32_t* seq_lens, int num_seqs, int num_kv_heads, int group,
+                             int head_dim, int gate, double threshold, int num_splits, int num_sms,
+                             void* out, int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
+                             uint8_t* mask_out, uint32_t* retained, uint32_t* status, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* Log-sum-exp merge of partial softmax states: for each of num_units rows,
+ * m (num_units, num_parts), l (num_units, num_parts) and acc (num_units,
+ * num_parts, head_dim), all float32 contiguous, m in log2 units as written
+ * by this library.  out[u] = sum_p acc[u,p] 2^(m[u,p]-M) / max(sum_p l[u,p]
+ * 2^(m[u,p]-M), 1e-9).  Used to combine sequence shards computed on
+ * different GPUs. */
+int oc_lse_merge(const float* m, const float* l, const float* acc, int64_t num_units, int num_parts,
+                 int head_dim, void* out, int out_dtype, void* stream);
+
+/* Sequence-shard decode: like oc_fused_attention_v3_gqa (num_seqs = 1) but
+ * instead of the final output it writes this shard's merged partial state
+ * m_out (units), l_out (units), acc_out (units, head_dim), units =
+ * num_kv_heads*group, for oc_lse_merge across shards.  The tau gate and the
+ * tile grid are those of the full sequence restricted to this shard. */
+int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_stride, const void* keys,
+                                int k_dtype, int64_t k_head_stride, int64_t k_tok_stride,
+                                const void* values, int v_dtype, int64_t v_head_stride,
+                                int64_t v_tok_stride, int num_kv_heads, int group, int64_t seq_len,
+                                int head_dim, double tau, int num_splits, int num_sms, float* m_out,
+                                float* l_out, float* acc_out, uint8_t* mask_out, uint32_t* retained,
+                                uint32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ORTHOCACHE_B200_H */

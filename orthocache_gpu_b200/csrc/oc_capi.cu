@@ -1,0 +1,322 @@
+// C ABI of liborthocache_b200.so: argument validation, the reference's
+// threshold semantics, split selection, and dispatch to the kernel
+// instantiations.  Declarations and contracts: include/orthocache_b200.h.
+#include <cmath>
+#include <cfloat>
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/orthocache_b200.h"
+#include "oc_decode.cuh"
+#include "oc_dispatch.h"
+
+namespace {
+
+using oc::DecodeParams;
+
+
+int elem_bytes(int dt) {
+  switch (dt) {
+    case OC_F32: return 4;
+    case OC_F16: case OC_BF16: return 2;
+    case OC_F8E4M3: return 1;
+    default: return 0;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Largest float32 <= x: the float threshold t with  (double)z > x  <=>  z > t
+// and  (double)z <= x  <=>  z <= t  for every float32 z.
+float round_down_f32(double x) {
+  if (std::isnan(x)) return NAN;
+  float f = static_cast<float>(x);
+  if (static_cast<double>(f) > x) f = std::nextafterf(f, -INFINITY);
+  return f;
+}
+
+int gc_for_group(int group) {
+  if (group <= 1) return 1;
+  if (group <= 2) return 2;
+  if (group <= 4) return 4;
+  return 8;
+}
+
+bool hd_supported(int hd, int k_dtype) {
+  if (hd != 16 && hd != 32 && hd != 64 && hd != 128 && hd != 256) return false;
+  if (k_dtype == OC_F32 && hd > 128) return false;
+  return true;
+}
+
+bool types_supported(int q_dtype, int k_dtype, int v_dtype, int out_dtype) {
+  auto qv = [](int d) { return d == OC_F32 || d == OC_F16 || d == OC_BF16; };
+  if (!qv(q_dtype) || !qv(out_dtype) || !qv(v_dtype)) return false;
+  if (k_dtype == OC_F8E4M3) return true;
+  return k_dtype == v_dtype;
+}
+
+int run(const DecodeParams& p, int k_dtype, int v_dtype, int hd, bool attn, cudaStream_t st) {
+  const int gc = gc_for_group(p.group);
+  switch (k_dtype) {
+    case OC_F32: return oc::dispatch_f32(p, v_dtype, hd, gc, attn, st);
+    case OC_F16: return oc::dispatch_f16(p, v_dtype, hd, gc, attn, st);
+    case OC_BF16: return oc::dispatch_bf16(p, v_dtype, hd, gc, attn, st);
+    case OC_F8E4M3: return oc::dispatch_f8(p, v_dtype, hd, gc, attn, st);
+    default: return OC_ERR_UNSUPPORTED;
+  }
+}
+
+int sms_or_device(int num_sms) {
+  if (num_sms > 0) return num_sms;
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 1;
+}
+
+// Fill the workspace part of DecodeParams; workspace layout:
+// [part_ml: units*S*2 floats][part_acc: units*S*hd floats][tickets: groups*chunks u32]
+int attach_workspace(DecodeParams& p, int64_t num_groups, int hd, void* ws, size_t ws_bytes) {
+  if (p.num_splits <= 1) return OC_OK;
+  const size_t need = oc_workspace_bytes(num_groups, p.group, p.num_splits, hd);
+  if (ws == nullptr || ws_bytes < need || !aligned16(ws)) return OC_ERR_WORKSPACE;
+  const int64_t units = num_groups * p.group;
+  char* b = static_cast<char*>(ws);
+  p.part_ml = reinterpret_cast<float*>(b);
+  b += sizeof(float) * units * p.num_splits * 2;
+  p.part_acc = reinterpret_cast<float*>(b);
+  b += sizeof(float) * units * p.num_splits * hd;
+  p.tickets = reinterpret_cast<uint32_t*>(b);
+  return OC_OK;
+}
+
+DecodeParams blank() {
+  DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.layout = oc::LAYOUT_LINEAR;
+  p.block_shift = 0;
+  p.num_seqs = 1;
+  p.group = 1;
+  return p;
+}
+
+bool stride_ok(int64_t stride_elems, int esz) { return ((stride_elems * esz) & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* oc_status_string(int code) {
+  switch (code) {
+    case OC_OK: return "ok";
+    case OC_ERR_INVALID: return "invalid argument (pointer, size, stride or 16-byte alignment)";
+    case OC_ERR_UNSUPPORTED: return "unsupported dtype / head_dim combination";
+    case OC_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+    case OC_ERR_CUDA: return "CUDA launch failed";
+    default: return "unknown status";
+  }
+}
+
+int oc_version(void) { return 100; }
+
+size_t oc_workspace_bytes(int64_t num_groups, int group, int num_splits, int head_dim) {
+  if (num_splits <= 1) return 0;
+  const int gc = gc_for_group(group);
+  const int64_t chunks = (group + gc - 1) / gc;
+  const int64_t units = num_groups * group;
+  size_t b = sizeof(float) * (size_t)units * num_splits * (2 + head_dim);
+  b += sizeof(uint32_t) * (size_t)(num_groups * chunks);
+  return (b + 255) & ~size_t(255);
+}
+
+int oc_auto_num_splits(int64_t num_tiles, int num_sms) {
+  int64_t max_splits = num_tiles / 4;
+  if (max_splits < 1) max_splits = 1;
+  int64_t s = num_sms;
+  if (max_splits < s) s = max_splits;
+  if (num_tiles < s) s = num_tiles;
+  return s < 1 ? 1 : (int)s;
+}
+
+int oc_fwht_eviction(const void* keys, int k_dtype, int64_t num_tokens, int head_dim, int64_t k_tok_stride,
+                     double zeta_max, uint8_t* mask_out, float* zeta_out, uint32_t* status, void* stream) {
+  const int kb = elem_bytes(k_dtype);
+  if (!keys || !mask_out || !status || kb == 0 || num_tokens < 0 || (num_tokens % 64) != 0)
+    return OC_ERR_INVALID;
+  if (!hd_supported(head_dim, k_dtype)) return OC_ERR_UNSUPPORTED;
+  if (!aligned16(keys) || !stride_ok(k_tok_stride, kb)) return OC_ERR_INVALID;
+  const int64_t tiles = num_tokens / 64;
+  if (tiles == 0) return OC_OK;
+  DecodeParams p = blank();
+  p.k = static_cast<const char*>(keys);
+  p.k_tok_stride = k_tok_stride * kb;
+  p.num_kv_heads = 1;
+  p.num_tiles = (int)tiles;
+  p.num_splits = oc_auto_num_splits(tiles, sms_or_device(0));
+  p.gate = oc::GATE_ZETA_MASK;
+  p.thr = static_cast<float>(zeta_max);  // torch compares a float32 tensor with the scalar in float32
+  p.mask = reinterpret_cast<int8_t*>(mask_out);
+  p.score = zeta_out;
+  p.status = status;
+  return run(p, k_dtype, k_dtype, head_dim, false, static_cast<cudaStream_t>(stream));
+}
+
+static int v3_common(DecodeParams& p, const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                     const void* keys, int k_dtype, int64_t k_seq_stride, int64_t k_head_stride,
+                     int64_t k_tok_stride, const void* values, int v_dtype, int64_t v_seq_stride,
+                     int64_t v_head_stride, int64_t v_tok_stride, int num_seqs, int num_kv_heads, int group,
+                     int64_t seq_len, int head_dim, int num_splits, int num_sms, void* out, int out_dtype,
+                     int64_t out_seq_stride, int64_t out_head_stride, uint8_t* mask_out, uint32_t* retained,
+                     uint32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
+  const int kb = elem_bytes(k_dtype), vb = elem_bytes(v_dtype);
+  if (!q || !keys || !values || !status || kb == 0 || vb == 0) return OC_ERR_INVALID;
+  if (num_seqs < 1 || num_kv_heads < 1 || group < 1 || seq_len < 0 || (seq_len % 64) != 0) return OC_ERR_INVALID;
+  if (!types_supported(q_dtype, k_dtype, v_dtype, out_dtype) || !hd_supported(head_dim, k_dtype))
+    return OC_ERR_UNSUPPORTED;
+  if (!aligned16(keys) || !aligned16(values)) return OC_ERR_INVALID;
+  if (!stride_ok(k_tok_stride, kb) || !stride_ok(v_tok_stride, vb) || !stride_ok(k_head_stride, kb) ||
+      !stride_ok(v_head_stride, vb) || !stride_ok(k_seq_stride, kb) || !stride_ok(v_seq_stride, vb))
+    return OC_ERR_INVALID;
+  const int64_t tiles = seq_len / 64;
+  if (tiles > INT32_MAX / 64) return OC_ERR_INVALID;
+  p.q = q;
+  p.q_dtype = q_dtype;
+  p.q_seq_stride = q_seq_stride;
+  p.q_head_stride = q_head_stride;
+  p.k = static_cast<const char*>(keys);
+  p.v = static_cast<const char*>(values);
+  p.k_seq_stride = k_seq_stride * kb;
+  p.k_head_stride = k_head_stride * kb;
+  p.k_tok_stride = k_tok_stride * kb;
+  p.v_seq_stride = v_seq_stride * vb;
+  p.v_head_stride = v_head_stride * vb;
+  p.v_tok_stride = v_tok_stride * vb;
+  p.num_seqs = num_seqs;
+  p.num_kv_heads = num_kv_heads;
+  p.group = group;
+  p.num_tiles = (int)tiles;
+  p.num_splits = num_splits > 0 ? num_splits : oc_auto_num_splits(tiles, sms_or_device(num_sms));
+  if (tiles > 0 && p.num_splits > tiles) p.num_splits = (int)tiles;
+  if (p.num_splits < 1) p.num_splits = 1;
+  if (p.num_splits > 65535) return OC_ERR_INVALID;
+  p.scale_log2 = static_cast<float>((1.0 / std::sqrt((double)head_dim)) * 1.4426950408889634);
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.out_seq_stride = out_seq_stride;
+  p.out_head_stride = out_head_stride;
+  p.mask = reinterpret_cast<int8_t*>(mask_out);
+  p.stats = retained;
+  p.status = status;
+  const int r = attach_workspace(p, (int64_t)num_seqs * num_kv_heads, head_dim, workspace, workspace_bytes);
+  if (r != OC_OK) return r;
+  if (p.sh_acc == nullptr && out == nullptr) return OC_ERR_INVALID;
+  return run(p, k_dtype, v_dtype, head_dim, true, static_cast<cudaStream_t>(stream));
+}
+
+int oc_fused_attention_v2(const void* q, int q_dtype, int64_t q_head_stride, const void* keys, int k_dtype,
+                          int64_t k_head_stride, int64_t k_tok_stride, const void* values, int v_dtype,
+                          int64_t v_head_stride, int64_t v_tok_stride, int num_heads, int64_t seq_len,
+                          int head_dim, double zeta_max, int num_splits, int num_sms, void* out, int out_dtype,
+                          int64_t out_head_stride, uint8_t* mask_out, uint32_t* retained, uint32_t* status,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  DecodeParams p = blank();
+  p.gate = oc::GATE_ZETA_ATTN;
+  p.thr = round_down_f32(zeta_max);
+  // V2 is the kv_heads = num_heads, group = 1 case of the generic decode
+  return v3_common(p, q, q_dtype, 0, q_head_stride, keys, k_dtype, 0, k_head_stride, k_tok_stride, values,
+                   v_dtype, 0, v_head_stride, v_tok_stride, 1, num_heads, 1, seq_len, head_dim, num_splits,
+                   num_sms, out, out_dtype, 0, out_head_stride, mask_out, retained, status, workspace,
+                   workspace_bytes, stream);
+}
+
+int oc_fused_attention_v1(const void* q, int q_dtype, const void* keys, int k_dtype, int64_t k_tok_stride,
+                          const void* values, int v_dtype, int64_t v_tok_stride, int64_t seq_len, int head_dim,
+                          double zeta_max, int num_sms, void* out, int out_dtype, uint8_t* mask_out,
+                          uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  return oc_fused_attention_v2(q, q_dtype, head_dim, keys, k_dtype, 0, k_tok_stride, values, v_dtype, 0,
+                               v_tok_stride, 1, seq_len, head_dim, zeta_max, 0, num_sms, out, out_dtype,
+                               head_dim, mask_out, retained, status, workspace, workspace_bytes, stream);
+}
+
+int oc_fused_attention_v3_gqa(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                              const void* keys, int k_dtype, int64_t k_seq_stride, int64_t k_head_stride,
+                              int64_t k_tok_stride, const void* values, int v_dtype, int64_t v_seq_stride,
+                              int64_t v_head_stride, int64_t v_tok_stride, int num_seqs, int num_kv_heads,
+                              int group, int64_t seq_len, int head_dim, double tau, int num_splits, int num_sms,
+                              void* out, int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
+                              uint8_t* mask_out, uint32_t* retained, uint32_t* status, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  DecodeParams p = blank();
+  p.gate = oc::GATE_CS;
+  p.thr = round_down_f32(tau);
+  return v3_common(p, q, q_dtype, q_seq_stride, q_head_stride, keys, k_dtype, k_seq_stride, k_head_stride,
+                   k_tok_stride, values, v_dtype, v_seq_stride, v_head_stride, v_tok_stride, num_seqs,
+                   num_kv_heads, group, seq_len, head_dim, num_splits, num_sms, out, out_dtype, out_seq_stride,
+                   out_head_stride, mask_out, retained, status, workspace, workspace_bytes, stream);
+}
+
+int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_stride, const void* keys, int k_dtype,
+                                int64_t k_head_stride, int64_t k_tok_stride, const void* values, int v_dtype,
+                                int64_t v_head_stride, int64_t v_tok_stride, int num_kv_heads, int group,
+                                int64_t seq_len, int head_dim, double tau, int num_splits, int num_sms,
+                                float* m_out, float* l_out, float* acc_out, uint8_t* mask_out,
+                                uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  if (!m_out || !l_out || !acc_out) return OC_ERR_INVALID;
+  DecodeParams p = blank();
+  p.gate = oc::GATE_CS;
+  p.thr = round_down_f32(tau);
+  p.sh_m = m_out;
+  p.sh_l = l_out;
+  p.sh_acc = acc_out;
+  return v3_common(p, q, q_dtype, 0, q_head_stride, keys, k_dtype, 0, k_head_stride, k_tok_stride, values,
+                   v_dtype, 0, v_head_stride, v_tok_stride, 1, num_kv_heads, group, seq_len, head_dim,
+                   num_splits, num_sms, nullptr, OC_F32, 0, head_dim, mask_out, retained, status, workspace,
+                   workspace_bytes, stream);
+}
+
+int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                             const void* k_cache, int k_dtype, int64_t k_blk_stride, int64_t k_head_stride,
+                             int64_t k_tok_stride, const void* v_cache, int v_dtype, int64_t v_blk_stride,
+                             int64_t v_head_stride, int64_t v_tok_stride, int num_blocks, int block_size,
+                             const int32_t* block_tables, int64_t bt_seq_stride, int max_blocks,
+                             const int32_t* seq_lens, int num_seqs, int num_kv_heads, int group, int head_dim,
+                             int gate, double threshold, int num_splits, int num_sms, void* out, int out_dtype,
+                             int64_t out_seq_stride, int64_t out_head_stride, uint8_t* mask_out,
+                             uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  if (!block_tables || block_size < 1 || (block_size & (block_size - 1)) || max_blocks < 0 || num_blocks < 1)
+    return OC_ERR_INVALID;
+  const int kb = elem_bytes(k_dtype), vb = elem_bytes(v_dtype);
+  if (kb == 0 || vb == 0) return OC_ERR_INVALID;
+  if (!stride_ok(k_blk_stride, kb) || !stride_ok(v_blk_stride, vb)) return OC_ERR_INVALID;
+  const int64_t tokens = (int64_t)max_blocks * block_size;
+  DecodeParams p = blank();
+  if (gate == OC_GATE_ZETA) {
+    p.gate = oc::GATE_ZETA_ATTN;
+  } else if (gate == OC_GATE_CAUCHY_SCHWARZ) {
+    p.gate = oc::GATE_CS;
+  } else {
+    return OC_ERR_INVALID;
+  }
+  p.thr = round_down_f32(threshold);
+  p.layout = oc::LAYOUT_PAGED;
+  p.block_tables = block_tables;
+  p.bt_seq_stride = bt_seq_stride;
+  p.k_blk_stride = k_blk_stride * kb;
+  p.v_blk_stride = v_blk_stride * vb;
+  int shift = 0;
+  while ((1 << shift) < block_size) ++shift;
+  p.block_shift = shift;
+  p.num_blocks = num_blocks;
+  p.seq_lens = seq_lens;
+  // the paged grid covers floor(max_blocks*block_size / 64) tiles per sequence
+  const int64_t seq_len = tokens - tokens % 64;
+  return v3_common(p, q, q_dtype, q_seq_stride, q_head_stride, k_cache, k_dtype, 0, k_head_stride, k_tok_stride,
+                   v_cache, v_dtype, 0, v_head_stride, v_tok_stride, num_seqs, num_kv_heads, group, seq_len,
+                   head_dim, num_splits, num_sms, out, out_dtype, out_seq_stride, out_head_stride, mask_out,
+                   retained, status, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,104 @@
+"""Generate the golden fixtures by running the reference's own CPU path.
+
+Run in a container where the reference source tree is available::
+
+    python tests/golden/make_golden.py /path/to/orthocache-gpu
+
+It imports ``orthocache_gpu`` from ``<ref>/src`` and calls the reference's
+CPU implementations (the ``_pytorch_*`` functions its public wrappers use
+without CUDA) on the inputs of ``cases.py``.  Outputs are stored in
+``tests/golden/<case>.npz`` together with the SHA-256 of the inputs.  The
+GPU box never runs this script; the tests only read the ``.npz`` files.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+sys.path.insert(0, HERE)
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, os.path.join(ref_root, "src"))
+    import torch
+    from orthocache_gpu.triton_kernels import fwht_fused_prototype as fw
+    from orthocache_gpu.triton_kernels import fused_eviction as fe
+    from orthocache_gpu.triton_kernels import gqa_eviction as ge
+    from orthocache_gpu.triton_kernels import paged_eviction as pe
+
+    from cases import CASES, case_inputs, digest, fp8_quantize
+
+    torch.set_flush_denormal(True)   # the reference's conftest does the same
+    torch.set_num_threads(1)
+    T = torch.from_numpy
+
+    for name in CASES:
+        inp = case_inputs(name)
+        out = {}
+        arrays = [v for v in inp.values() if isinstance(v, np.ndarray)]
+        out["input_sha256"] = np.array(digest(*arrays))
+        out["torch_version"] = np.array(torch.__version__)
+        ths = inp["thresholds"]
+        out["thresholds"] = np.array(ths, np.float64)
+        if name.startswith("mask"):
+            for i, z in enumerate(ths):
+                m, zeta = fw._pytorch_fwht_eviction(T(inp["keys"]), z, return_zeta=True)
+                out[f"mask_{i}"] = m.numpy()
+                out[f"zeta_{i}"] = zeta.numpy()
+        elif name == "v1_config1":
+            for i, z in enumerate(ths):
+                o, meta = fe.fused_orthocache_attention(
+                    T(inp["q"]), T(inp["keys"]), T(inp["values"]), z, return_mask=True)
+                out[f"out_{i}"] = o.numpy()
+                out[f"mask_{i}"] = meta["eviction_mask"].numpy()
+                out[f"retained_{i}"] = np.array(meta["tiles_retained"])
+        elif name in ("v2_f16", "v2_bf16_hd64"):
+            dt = getattr(torch, inp["dtype"])
+            q, k, v = (T(inp[x]).to(dt) for x in ("q", "keys", "values"))
+            for i, z in enumerate(ths):
+                # internal CPU path keeps the fp32 output (public wrapper casts to dtype)
+                o32, meta = fe._pytorch_fused_orthocache_multihead(q, k, v, z)
+                o, _ = fe.fused_orthocache_attention_v2(q, k, v, z)
+                out[f"out32_{i}"] = o32.numpy()
+                out[f"out_{i}"] = o.float().numpy()
+                out[f"retained_{i}"] = np.array(meta["tiles_retained"])
+                masks = [fw._pytorch_fwht_eviction(k[h], z, return_zeta=True) for h in range(k.shape[0])]
+                out[f"zeta_{i}"] = np.stack([m[1].numpy() for m in masks])
+        elif name.startswith("v3"):
+            dt = getattr(torch, inp["dtype"])
+            q, k, v = (T(inp[x]).to(dt) for x in ("q", "keys", "values"))
+            g = inp["group"]
+            for i, tau in enumerate(ths):
+                o32, meta = ge._pytorch_gqa_cauchy_schwarz_attention(q, k, v, tau, g)
+                o, _ = ge.fused_orthocache_attention_v3_gqa(q, k, v, tau, g)
+                out[f"out32_{i}"] = o32.numpy()
+                out[f"out_{i}"] = o.float().numpy()
+                out[f"retained_{i}"] = np.array(meta["tiles_retained"])
+                out[f"evicted_{i}"] = np.array(meta["tiles_evicted"])
+        elif name == "paged_f32":
+            q, kc, vc = T(inp["q"]), T(inp["k_cache"]), T(inp["v_cache"])
+            bt = T(inp["block_tables"])
+            for i, z in enumerate(ths):
+                o, _ = pe.fused_orthocache_attention_paged(q, kc, vc, bt, z)
+                out[f"out_{i}"] = o.numpy()
+        elif name == "v2_fp8":
+            k8, scale = fp8_quantize(inp["keys"])
+            q, v = T(inp["q"]), T(inp["values"])
+            out["k_scale"] = np.array(scale)
+            out["keys_fp8_bits"] = k8.view(torch.uint8).numpy()
+            for i, z in enumerate(ths):
+                o, _ = fe.fused_orthocache_attention_v2(q, k8, v, z, k_scale=scale)
+                out[f"out_{i}"] = o.numpy()
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+        print("wrote", name)
+
+
+if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <reference project root>")
+    main(sys.argv[1])

@@ -1,0 +1,116 @@
+"""CPU tests of the host layer: assertion messages, C-ABI exports, no CPU fallback."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import orthocache_gpu_b200 as oc
+from orthocache_gpu_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "orthocache_b200.h")).read()
+    return sorted(set(re.findall(r"^\s*(?:const char\*|int|size_t)\s+(oc_\w+)\(", src, re.M)))
+
+
+def test_header_declares_the_reference_entry_points():
+    names = declared_symbols()
+    for n in ["oc_fwht_eviction", "oc_fused_attention_v1", "oc_fused_attention_v2",
+              "oc_fused_attention_v3_gqa", "oc_fused_attention_paged", "oc_lse_merge"]:
+        assert n in names
+
+
+@pytest.mark.skipif(not os.path.exists(_lib.LIB_PATH), reason="library not built")
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    # every binding signature names a declared symbol
+    assert set(_lib.SIGNATURES) <= set(declared_symbols())
+    l = _lib.load()
+    assert l.oc_version() >= 100
+    assert l.oc_auto_num_splits(512, 148) == 128      # the reference heuristic
+    assert l.oc_auto_num_splits(16, 148) == 4
+    assert l.oc_auto_num_splits(0, 148) == 1
+    assert l.oc_auto_num_splits(10000, 148) == 148
+    assert l.oc_workspace_bytes(32, 1, 1, 128) == 0
+    assert l.oc_workspace_bytes(32, 1, 128, 128) >= 32 * 128 * 130 * 4
+    assert l.oc_status_string(3).decode().startswith("workspace")
+
+
+@pytest.mark.skipif(not os.path.exists(_lib.LIB_PATH), reason="library not built")
+def test_c_abi_rejects_bad_arguments_without_a_gpu():
+    l = _lib.load()
+    # null pointers / bad sizes are rejected before any CUDA call
+    assert l.oc_fwht_eviction(None, 1, 128, 128, 128, 5.0, None, None, None, None) == 1
+    assert l.oc_lse_merge(None, None, None, 1, 1, 128, None, 0, None) == 1
+    # unsupported head_dim
+    buf = ctypes.create_string_buffer(64 * 1024 + 16)
+    addr = (ctypes.addressof(buf) + 15) & ~15
+    st = ctypes.c_uint32(0)
+    assert l.oc_fwht_eviction(addr, 1, 64, 100, 100, 5.0, addr, None, ctypes.addressof(st), None) == 2
+
+
+def _t(*shape):
+    return torch.randn(*shape)
+
+
+def test_v1_assertions_match_reference_messages():
+    q, k, v = _t(1, 128), _t(256, 128), _t(256, 128)
+    with pytest.raises(AssertionError, match="head_dim.*must be a power of 2"):
+        oc.fused_orthocache_attention(_t(1, 100), _t(256, 100), _t(256, 100), zeta_max=5.0)
+    with pytest.raises(AssertionError, match="tile_size.*must be a power of 2"):
+        oc.fused_orthocache_attention(q, k, v, zeta_max=5.0, tile_size=50)
+    with pytest.raises(AssertionError, match="not divisible by tile_size"):
+        oc.fused_orthocache_attention(q, _t(250, 128), _t(250, 128), zeta_max=5.0)
+    with pytest.raises(AssertionError, match=r"q must be \(1, head_dim\)"):
+        oc.fused_orthocache_attention(_t(2, 128), k, v, zeta_max=5.0)
+
+
+def test_v2_v3_paged_assertions_match_reference_messages():
+    with pytest.raises(AssertionError, match="num_splits.*greater than 0"):
+        oc.fused_orthocache_attention_v2(_t(2, 64), _t(2, 128, 64), _t(2, 128, 64), 5.0, num_splits=0)
+    with pytest.raises(AssertionError, match="not divisible by tile_size"):
+        oc.fused_orthocache_attention_v2(_t(2, 64), _t(2, 100, 64), _t(2, 100, 64), 5.0)
+    with pytest.raises(AssertionError, match="num_query_heads"):
+        oc.fused_orthocache_attention_v3_gqa(_t(6, 64), _t(2, 128, 64), _t(2, 128, 64), 1.0, num_query_groups=4)
+    bt = torch.tensor([[0, 1]], dtype=torch.int32)
+    with pytest.raises(AssertionError, match="head_dim.*power of 2"):
+        oc.fused_orthocache_attention_paged(_t(1, 2, 63), _t(4, 2, 32, 63), _t(4, 2, 32, 63), bt, zeta_max=5.0)
+    with pytest.raises(AssertionError, match="block_size.*power of 2"):
+        oc.fused_orthocache_attention_paged(_t(1, 2, 64), _t(4, 2, 31, 64), _t(4, 2, 31, 64), bt, zeta_max=5.0)
+
+
+def test_no_cpu_fallback():
+    q, k, v = _t(1, 128), _t(256, 128), _t(256, 128)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        oc.fused_orthocache_attention(q, k, v, zeta_max=5.0)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        oc.fused_orthocache_attention_v2(_t(2, 128), _t(2, 256, 128), _t(2, 256, 128), 5.0)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        oc.triton_fwht_eviction(k, 5.0)
+
+
+def test_other_tile_sizes_are_refused_clearly():
+    with pytest.raises(NotImplementedError, match="64-token tile"):
+        oc.fused_orthocache_attention_v2(_t(2, 64), _t(2, 128, 64), _t(2, 128, 64), 5.0, tile_size=32)
+
+
+def test_walsh_matrix_matches_oracle():
+    from oracle import orthocache_oracle as orc
+    import numpy as np
+    for n in (8, 64):
+        np.testing.assert_array_equal(oc.generate_walsh_matrix(n).numpy(), orc.walsh_matrix(n))
+
+
+def test_pipeline_dense_mode_runs_on_cpu_and_compact_is_out_of_scope():
+    q, k, v = _t(1, 4, 64), _t(256, 4, 64), _t(256, 4, 64)
+    out, meta = oc.orthocache_forward(q, k, v, mode="dense")
+    assert out.shape == (1, 4, 64) and meta["actual_mode"] == "dense" and meta["eviction_rate"] == 0.0
+    with pytest.raises(NotImplementedError):
+        oc.orthocache_forward(q, k, v, mode="compact")
