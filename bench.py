@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=SEQ)
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--quick", action="store_true",
+                    help="timed steps only: no sweep, e2e or CPU baseline (profiling target)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-sample-heads", type=int, default=0, help="0 = auto (about 10-30 s of CPU work)")
     return ap.parse_args()
@@ -286,6 +288,11 @@ def main():
     achieved = per_step_bytes / (launch_us * 1e-6) / 1e9
     peak, peak_kind = measured_peaks()
 
+    if a.quick:
+        if rank == 0:
+            print(json.dumps({"metric": metric, "value": round(value, 1), "unit": "GB/s", "steps": steps,
+                              "launch_us": round(launch_us, 3), "achieved": round(achieved, 1)}))
+        return
     # e2e: public API, pinned host inputs -> device -> kernel -> host output
     hq, hk, hv = (t_.cpu().pin_memory() for t_ in (q, k, v))
     h2d = hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2

@@ -27,7 +27,8 @@
  * Thresholds are given in double precision and compared exactly as the
  * reference's CPU path compares them (see the notes at each function).
  *
- * Workspace: split-K partials and merge tickets.  Size it with
+ * Workspace: merge tickets (a fixed 256 KiB region at its start) and the
+ * split-K partials.  Size it with
  * oc_workspace_bytes(); it must be zero-filled once before first use and is
  * left zeroed by every successful launch.  Launches that share a workspace
  * must not overlap on the GPU.  A non-zero *status word after a launch

@@ -74,19 +74,29 @@ int sms_or_device(int num_sms) {
   return n > 0 ? n : 1;
 }
 
-// Fill the workspace part of DecodeParams; workspace layout:
-// [part_ml: units*S*2 floats][part_acc: units*S*hd floats][tickets: groups*chunks u32]
+// Fill the workspace part of DecodeParams.  Layout:
+// [tickets: kMaxTickets u32, fixed][part_ml: units*S*2 floats][part_acc: units*S*hd floats],
+// each region padded to 256 bytes.
+// The ticket region has a fixed size and offset so that launches with
+// different shapes never read another launch's partials as tickets; every
+// successful launch leaves its tickets at zero.
+constexpr int64_t kMaxTickets = 65536;
+constexpr size_t pad256(size_t b) { return (b + 255) & ~size_t(255); }
+constexpr size_t kTicketBytes = sizeof(uint32_t) * kMaxTickets;
+
 int attach_workspace(DecodeParams& p, int64_t num_groups, int hd, void* ws, size_t ws_bytes) {
   if (p.num_splits <= 1) return OC_OK;
+  const int gc = gc_for_group(p.group);
+  if (num_groups * ((p.group + gc - 1) / gc) > kMaxTickets) return OC_ERR_INVALID;
   const size_t need = oc_workspace_bytes(num_groups, p.group, p.num_splits, hd);
   if (ws == nullptr || ws_bytes < need || !aligned16(ws)) return OC_ERR_WORKSPACE;
   const int64_t units = num_groups * p.group;
   char* b = static_cast<char*>(ws);
-  p.part_ml = reinterpret_cast<float*>(b);
-  b += sizeof(float) * units * p.num_splits * 2;
-  p.part_acc = reinterpret_cast<float*>(b);
-  b += sizeof(float) * units * p.num_splits * hd;
   p.tickets = reinterpret_cast<uint32_t*>(b);
+  b += kTicketBytes;
+  p.part_ml = reinterpret_cast<float*>(b);
+  b += pad256(sizeof(float) * units * p.num_splits * 2);
+  p.part_acc = reinterpret_cast<float*>(b);  // 256-byte aligned: the merge reads it as float4
   return OC_OK;
 }
 
@@ -121,12 +131,9 @@ int oc_version(void) { return 100; }
 
 size_t oc_workspace_bytes(int64_t num_groups, int group, int num_splits, int head_dim) {
   if (num_splits <= 1) return 0;
-  const int gc = gc_for_group(group);
-  const int64_t chunks = (group + gc - 1) / gc;
   const int64_t units = num_groups * group;
-  size_t b = sizeof(float) * (size_t)units * num_splits * (2 + head_dim);
-  b += sizeof(uint32_t) * (size_t)(num_groups * chunks);
-  return (b + 255) & ~size_t(255);
+  return kTicketBytes + pad256(sizeof(float) * (size_t)units * num_splits * 2) +
+         pad256(sizeof(float) * (size_t)units * num_splits * head_dim);
 }
 
 int oc_auto_num_splits(int64_t num_tiles, int num_sms) {
@@ -169,11 +176,12 @@ static int v3_common(DecodeParams& p, const void* q, int q_dtype, int64_t q_seq_
                      int64_t out_seq_stride, int64_t out_head_stride, uint8_t* mask_out, uint32_t* retained,
                      uint32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
   const int kb = elem_bytes(k_dtype), vb = elem_bytes(v_dtype);
-  if (!q || !keys || !values || !status || kb == 0 || vb == 0) return OC_ERR_INVALID;
+  if (!q || !status || kb == 0 || vb == 0) return OC_ERR_INVALID;
+  if (seq_len > 0 && (!keys || !values)) return OC_ERR_INVALID;
   if (num_seqs < 1 || num_kv_heads < 1 || group < 1 || seq_len < 0 || (seq_len % 64) != 0) return OC_ERR_INVALID;
   if (!types_supported(q_dtype, k_dtype, v_dtype, out_dtype) || !hd_supported(head_dim, k_dtype))
     return OC_ERR_UNSUPPORTED;
-  if (!aligned16(keys) || !aligned16(values)) return OC_ERR_INVALID;
+  if (!aligned16(keys) || !aligned16(values)) return OC_ERR_INVALID;  // null is aligned
   if (!stride_ok(k_tok_stride, kb) || !stride_ok(v_tok_stride, vb) || !stride_ok(k_head_stride, kb) ||
       !stride_ok(v_head_stride, vb) || !stride_ok(k_seq_stride, kb) || !stride_ok(v_seq_stride, vb))
     return OC_ERR_INVALID;
