@@ -52,7 +52,8 @@ enum {
   OC_ERR_INVALID = 1,     /* bad pointer, size, stride or alignment */
   OC_ERR_UNSUPPORTED = 2, /* dtype / head_dim combination not compiled */
   OC_ERR_WORKSPACE = 3,   /* workspace too small */
-  OC_ERR_CUDA = 4         /* the launch failed; see cudaGetLastError */
+  OC_ERR_CUDA = 4,        /* the launch failed; see cudaGetLastError */
+  OC_ERR_TOO_LARGE = 5    /* beyond the fixed scratch of oc_fused_attention_v2_noalloc */
 };
 
 /* bits of the device status word */
@@ -162,6 +163,28 @@ int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_strid
                                 int head_dim, double tau, int num_splits, int num_sms, float* m_out,
                                 float* l_out, float* acc_out, uint8_t* mask_out, uint32_t* retained,
                                 uint32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Allocation-free variant of oc_fused_attention_v2 (no counterpart in the
+ * reference).  For callers that cannot allocate device memory: code running
+ * inside another framework's allocator, under a memory budget, or from a
+ * plugin interface that hands over only inputs and outputs.  Same arguments
+ * and results as oc_fused_attention_v2 minus the workspace: the split-K
+ * scratch lives in a 32 MiB array that this library reserves statically on
+ * every GPU that loads it, held until the process exits.  A call whose
+ * scratch would exceed 32 MiB returns OC_ERR_TOO_LARGE (roughly: heads *
+ * splits * (head_dim + 2) * 4 bytes + 256 KiB).  It calls no cudaMalloc or
+ * cudaFree.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture.  Every call zeroes the array's merge
+ * tickets on the stream, and all calls share the one array: calls that
+ * overlap on the GPU (different streams, or different host threads) race
+ * and give wrong results. */
+int oc_fused_attention_v2_noalloc(const void* q, int q_dtype, int64_t q_head_stride,
+                                  const void* keys, int k_dtype, int64_t k_head_stride, int64_t k_tok_stride,
+                                  const void* values, int v_dtype, int64_t v_head_stride, int64_t v_tok_stride,
+                                  int num_heads, int64_t seq_len, int head_dim, double zeta_max,
+                                  int num_splits, int num_sms, void* out, int out_dtype, int64_t out_head_stride,
+                                  uint8_t* mask_out, uint32_t* retained, uint32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -123,6 +123,8 @@ const char* oc_status_string(int code) {
     case OC_ERR_UNSUPPORTED: return "unsupported dtype / head_dim combination";
     case OC_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
     case OC_ERR_CUDA: return "CUDA launch failed";
+    case OC_ERR_TOO_LARGE:
+      return "problem needs more scratch than the fixed 32 MiB of oc_fused_attention_v2_noalloc";
     default: return "unknown status";
   }
 }
@@ -328,3 +330,8 @@ int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, i
 }
 
 }  // extern "C"
+
+namespace oc {
+// Bytes at the start of a workspace that must be zero when a launch begins.
+size_t workspace_header_bytes() { return kTicketBytes; }
+}  // namespace oc

@@ -3,6 +3,7 @@
 // launch error.
 #pragma once
 #include <cuda_runtime.h>
+#include <cstddef>
 
 namespace oc {
 struct DecodeParams;
@@ -10,4 +11,5 @@ int dispatch_f32(const DecodeParams& p, int v_dtype, int hd, int gc, bool attn, 
 int dispatch_f16(const DecodeParams& p, int v_dtype, int hd, int gc, bool attn, cudaStream_t st);
 int dispatch_bf16(const DecodeParams& p, int v_dtype, int hd, int gc, bool attn, cudaStream_t st);
 int dispatch_f8(const DecodeParams& p, int v_dtype, int hd, int gc, bool attn, cudaStream_t st);
+size_t workspace_header_bytes();
 }  // namespace oc
