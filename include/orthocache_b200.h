@@ -27,13 +27,13 @@
  * Thresholds are given in double precision and compared exactly as the
  * reference's CPU path compares them (see the notes at each function).
  *
- * Workspace: merge tickets (a fixed 256 KiB region at its start) and the
- * split-K partials.  Size it with
- * oc_workspace_bytes(); it must be zero-filled once before first use and is
- * left zeroed by every successful launch.  Launches that share a workspace
- * must not overlap on the GPU.  A non-zero *status word after a launch
- * (OC_STATUS_*) means the outputs of that launch are invalid; re-zero the
- * workspace before reusing it.
+ * Workspace: a fixed header (grid-barrier counters, per-unit counts and merge
+ * tickets) followed by per-call scratch (retained-tile list, their logits,
+ * split partial states).  Size it with oc_workspace_bytes(); it must be
+ * zero-filled once before first use and every launch leaves the header zeroed
+ * again.  Launches that share a workspace must not overlap on the GPU.  A
+ * non-zero *status word after a launch (OC_STATUS_*) means the outputs of that
+ * launch are invalid; re-zero the workspace before reusing it.
  */
 #ifndef ORTHOCACHE_B200_H
 #define ORTHOCACHE_B200_H
@@ -67,10 +67,10 @@ const char* oc_status_string(int code);
 /* Library version, e.g. 100 for 0.1.0. */
 int oc_version(void);
 
-/* Bytes of workspace for a launch over `num_groups` (sequence, kv-head)
- * pairs with `group` query heads each, `num_splits` splits and `head_dim`.
- * Zero when num_splits == 1. */
-size_t oc_workspace_bytes(int64_t num_groups, int group, int num_splits, int head_dim);
+/* Bytes of workspace for an attention call over `num_groups` (sequence,
+ * kv-head) pairs with `group` query heads each, at most `num_tiles` 64-token
+ * tiles per sequence, and `head_dim`.  The mask-only call needs none. */
+size_t oc_workspace_bytes(int64_t num_groups, int group, int64_t num_tiles, int head_dim);
 
 /* The reference's split heuristic: min(num_sms, max(1, num_tiles/4), num_tiles),
  * at least 1 (fused_eviction.py:556-570). */
@@ -172,7 +172,7 @@ int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_strid
  * scratch lives in a 32 MiB array that this library reserves statically on
  * every GPU that loads it, held until the process exits.  A call whose
  * scratch would exceed 32 MiB returns OC_ERR_TOO_LARGE (roughly: heads *
- * splits * (head_dim + 2) * 4 bytes + 256 KiB).  It calls no cudaMalloc or
+ * tiles * 260 bytes + 1.4 MiB at head_dim 128).  It calls no cudaMalloc or
  * cudaFree.  The first call on each device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make that first
  * call before any stream capture.  Every call zeroes the array's merge

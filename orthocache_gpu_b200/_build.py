@@ -2,8 +2,8 @@
 
 Each ``csrc/*.cu`` translation unit is compiled by ``nvcc`` in parallel and
 linked into one shared library whose exported symbols are the C ABI of
-``include/orthocache_b200.h``.  Rebuilds only when a source is newer than
-the library.
+``include/orthocache_b200.h``.  Objects are kept beside the library and a
+translation unit is recompiled only when it or a header changed.
 """
 
 from __future__ import annotations
@@ -55,8 +55,13 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     cc = nvcc()
     objs = []
 
+    headers = [f for f in _deps() if not f.endswith(".cu")]
+    newest_header = max(os.path.getmtime(f) for f in headers)
+
     def compile_one(src):
         obj = os.path.join(OUT_DIR, os.path.basename(src)[:-3] + ".o")
+        if not force and os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(src), newest_header):
+            return obj
         cmd = [cc, *ARCH, *FLAGS, "-c", src, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
@@ -73,8 +78,6 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, LIB)
-    for o in objs:
-        os.remove(o)
     return LIB
 
 

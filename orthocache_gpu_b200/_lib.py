@@ -30,7 +30,7 @@ _vp, _i, _i64, _d, _sz = C.c_void_p, C.c_int, C.c_int64, C.c_double, C.c_size_t
 SIGNATURES = {
     "oc_status_string": (C.c_char_p, [_i]),
     "oc_version": (_i, []),
-    "oc_workspace_bytes": (_sz, [_i64, _i, _i, _i]),
+    "oc_workspace_bytes": (_sz, [_i64, _i, _i64, _i]),
     "oc_auto_num_splits": (_i, [_i64, _i]),
     "oc_fwht_eviction": (_i, [_vp, _i, _i64, _i, _i64, _d, _vp, _vp, _vp, _vp]),
     "oc_fused_attention_v2": (_i, [_vp, _i, _i64, _vp, _i, _i64, _i64, _vp, _i, _i64, _i64, _i, _i64, _i, _d,

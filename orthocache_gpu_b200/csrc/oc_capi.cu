@@ -55,15 +55,25 @@ bool types_supported(int q_dtype, int k_dtype, int v_dtype, int out_dtype) {
   return k_dtype == v_dtype;
 }
 
-int run(const DecodeParams& p, int k_dtype, int v_dtype, int hd, bool attn, cudaStream_t st) {
+int run(const DecodeParams& p, int k_dtype, int v_dtype, int hd, bool attn, int sms, cudaStream_t st) {
   const int gc = gc_for_group(p.group);
+#define OC_HDS(K, ...)                                              \
+  switch (hd) {                                                     \
+    case 16: return oc::dispatch_##K##_16(p, v_dtype, gc, attn, sms, st);   \
+    case 32: return oc::dispatch_##K##_32(p, v_dtype, gc, attn, sms, st);   \
+    case 64: return oc::dispatch_##K##_64(p, v_dtype, gc, attn, sms, st);   \
+    case 128: return oc::dispatch_##K##_128(p, v_dtype, gc, attn, sms, st); \
+    __VA_ARGS__                                                     \
+    default: return OC_ERR_UNSUPPORTED;                             \
+  }
   switch (k_dtype) {
-    case OC_F32: return oc::dispatch_f32(p, v_dtype, hd, gc, attn, st);
-    case OC_F16: return oc::dispatch_f16(p, v_dtype, hd, gc, attn, st);
-    case OC_BF16: return oc::dispatch_bf16(p, v_dtype, hd, gc, attn, st);
-    case OC_F8E4M3: return oc::dispatch_f8(p, v_dtype, hd, gc, attn, st);
+    case OC_F32: OC_HDS(f32)
+    case OC_F16: OC_HDS(f16, case 256: return oc::dispatch_f16_256(p, v_dtype, gc, attn, sms, st);)
+    case OC_BF16: OC_HDS(bf16, case 256: return oc::dispatch_bf16_256(p, v_dtype, gc, attn, sms, st);)
+    case OC_F8E4M3: OC_HDS(f8, case 256: return oc::dispatch_f8_256(p, v_dtype, gc, attn, sms, st);)
     default: return OC_ERR_UNSUPPORTED;
   }
+#undef OC_HDS
 }
 
 int sms_or_device(int num_sms) {
@@ -74,29 +84,47 @@ int sms_or_device(int num_sms) {
   return n > 0 ? n : 1;
 }
 
-// Fill the workspace part of DecodeParams.  Layout:
-// [tickets: kMaxTickets u32, fixed][part_ml: units*S*2 floats][part_acc: units*S*hd floats],
-// each region padded to 256 bytes.
-// The ticket region has a fixed size and offset so that launches with
-// different shapes never read another launch's partials as tickets; every
-// successful launch leaves its tickets at zero.
-constexpr int64_t kMaxTickets = 65536;
+// Workspace layout (every region 256-byte aligned):
+//   fixed header (kFixedBytes, zero between launches):
+//     [0, 256)             grid-barrier counters
+//     [256, +4*kMaxUnits)  retained tiles per unit
+//     [.., +4*kMaxUnits)   merge tickets per unit
+//   cnt_warp  kMaxWarps u32
+//   list      units*num_tiles i32
+//   part      2*kMaxWarps*gc*(hd+4) f32
+//   lg        units*num_tiles*gc*64 f32
+constexpr int64_t kMaxUnits = 2048;  // units per launch (shared-memory prefix arrays)
+constexpr int64_t kMaxWarps = 1280;
 constexpr size_t pad256(size_t b) { return (b + 255) & ~size_t(255); }
-constexpr size_t kTicketBytes = sizeof(uint32_t) * kMaxTickets;
+constexpr size_t kFixedBytes = pad256(256 + 2 * 4 * kMaxUnits);
 
-int attach_workspace(DecodeParams& p, int64_t num_groups, int hd, void* ws, size_t ws_bytes) {
-  if (p.num_splits <= 1) return OC_OK;
+struct WsLayout {
+  size_t cnt_warp, list, part, lg, total;
+};
+
+WsLayout ws_layout(int64_t units, int gc, int64_t num_tiles, int hd) {
+  WsLayout L;
+  const int64_t n = units * num_tiles;
+  L.cnt_warp = kFixedBytes;
+  L.list = L.cnt_warp + pad256(4 * kMaxWarps);
+  L.part = L.list + pad256(4 * (size_t)n);
+  L.lg = L.part + pad256(4 * (size_t)2 * kMaxWarps * gc * (hd + 4));
+  L.total = L.lg + pad256(4 * (size_t)n * gc * 64);
+  return L;
+}
+
+int attach_workspace(DecodeParams& p, int64_t units, int hd, void* ws, size_t ws_bytes) {
   const int gc = gc_for_group(p.group);
-  if (num_groups * ((p.group + gc - 1) / gc) > kMaxTickets) return OC_ERR_INVALID;
-  const size_t need = oc_workspace_bytes(num_groups, p.group, p.num_splits, hd);
-  if (ws == nullptr || ws_bytes < need || !aligned16(ws)) return OC_ERR_WORKSPACE;
-  const int64_t units = num_groups * p.group;
+  const WsLayout L = ws_layout(units, gc, p.num_tiles, hd);
+  if (ws == nullptr || ws_bytes < L.total || !aligned16(ws)) return OC_ERR_WORKSPACE;
   char* b = static_cast<char*>(ws);
-  p.tickets = reinterpret_cast<uint32_t*>(b);
-  b += kTicketBytes;
-  p.part_ml = reinterpret_cast<float*>(b);
-  b += pad256(sizeof(float) * units * p.num_splits * 2);
-  p.part_acc = reinterpret_cast<float*>(b);  // 256-byte aligned: the merge reads it as float4
+  p.gbar = reinterpret_cast<uint32_t*>(b);
+  p.cnt_unit = reinterpret_cast<uint32_t*>(b + 256);
+  p.tickets = reinterpret_cast<uint32_t*>(b + 256 + 4 * kMaxUnits);
+  p.cnt_warp = reinterpret_cast<uint32_t*>(b + L.cnt_warp);
+  p.list = reinterpret_cast<int32_t*>(b + L.list);
+  p.part = reinterpret_cast<float*>(b + L.part);
+  p.lg = reinterpret_cast<float*>(b + L.lg);
   return OC_OK;
 }
 
@@ -131,11 +159,12 @@ const char* oc_status_string(int code) {
 
 int oc_version(void) { return 100; }
 
-size_t oc_workspace_bytes(int64_t num_groups, int group, int num_splits, int head_dim) {
-  if (num_splits <= 1) return 0;
-  const int64_t units = num_groups * group;
-  return kTicketBytes + pad256(sizeof(float) * (size_t)units * num_splits * 2) +
-         pad256(sizeof(float) * (size_t)units * num_splits * head_dim);
+size_t oc_workspace_bytes(int64_t num_groups, int group, int64_t num_tiles, int head_dim) {
+  if (num_groups < 1 || group < 1 || num_tiles < 0 || head_dim < 1) return 0;
+  const int gc = gc_for_group(group);
+  int64_t units = num_groups * ((group + gc - 1) / gc);
+  if (units > kMaxUnits) units = kMaxUnits;  // larger batches run as several launches
+  return ws_layout(units, gc, num_tiles, head_dim).total;
 }
 
 int oc_auto_num_splits(int64_t num_tiles, int num_sms) {
@@ -167,7 +196,7 @@ int oc_fwht_eviction(const void* keys, int k_dtype, int64_t num_tokens, int head
   p.mask = reinterpret_cast<int8_t*>(mask_out);
   p.score = zeta_out;
   p.status = status;
-  return run(p, k_dtype, k_dtype, head_dim, false, static_cast<cudaStream_t>(stream));
+  return run(p, k_dtype, k_dtype, head_dim, false, sms_or_device(0), static_cast<cudaStream_t>(stream));
 }
 
 static int v3_common(DecodeParams& p, const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
@@ -217,10 +246,35 @@ static int v3_common(DecodeParams& p, const void* q, int q_dtype, int64_t q_seq_
   p.mask = reinterpret_cast<int8_t*>(mask_out);
   p.stats = retained;
   p.status = status;
-  const int r = attach_workspace(p, (int64_t)num_seqs * num_kv_heads, head_dim, workspace, workspace_bytes);
-  if (r != OC_OK) return r;
   if (p.sh_acc == nullptr && out == nullptr) return OC_ERR_INVALID;
-  return run(p, k_dtype, v_dtype, head_dim, true, static_cast<cudaStream_t>(stream));
+  const int sms = sms_or_device(num_sms);
+  const int gc = gc_for_group(group);
+  const int64_t units_per_seq = (int64_t)num_kv_heads * ((group + gc - 1) / gc);
+  if (units_per_seq > kMaxUnits) return OC_ERR_INVALID;
+  // the kernel keeps per-unit prefix arrays in shared memory: batches of at
+  // most kMaxUnits units run as consecutive launches on the stream
+  const int64_t seqs_per_launch = kMaxUnits / units_per_seq;
+  const int qsz = elem_bytes(q_dtype), osz = elem_bytes(out_dtype);
+  for (int64_t s0 = 0; s0 < num_seqs; s0 += seqs_per_launch) {
+    DecodeParams pc = p;
+    const int64_t ns = (num_seqs - s0) < seqs_per_launch ? (num_seqs - s0) : seqs_per_launch;
+    pc.num_seqs = (int)ns;
+    pc.q = static_cast<const char*>(q) + s0 * q_seq_stride * qsz;
+    if (p.layout == oc::LAYOUT_LINEAR) {
+      if (pc.k) pc.k += s0 * p.k_seq_stride;
+      if (pc.v) pc.v += s0 * p.v_seq_stride;
+    } else {
+      pc.block_tables = p.block_tables + s0 * p.bt_seq_stride;
+      if (p.seq_lens) pc.seq_lens = p.seq_lens + s0;
+    }
+    if (out) pc.out = static_cast<char*>(out) + s0 * out_seq_stride * osz;
+    if (p.mask) pc.mask = p.mask + s0 * num_kv_heads * tiles;
+    const int r = attach_workspace(pc, ns * units_per_seq, head_dim, workspace, workspace_bytes);
+    if (r != OC_OK) return r;
+    const int e = run(pc, k_dtype, v_dtype, head_dim, true, sms, static_cast<cudaStream_t>(stream));
+    if (e != OC_OK) return e;
+  }
+  return OC_OK;
 }
 
 int oc_fused_attention_v2(const void* q, int q_dtype, int64_t q_head_stride, const void* keys, int k_dtype,
@@ -333,5 +387,5 @@ int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, i
 
 namespace oc {
 // Bytes at the start of a workspace that must be zero when a launch begins.
-size_t workspace_header_bytes() { return kTicketBytes; }
+size_t workspace_header_bytes() { return kFixedBytes; }
 }  // namespace oc

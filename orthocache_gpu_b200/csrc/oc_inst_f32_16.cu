@@ -1,5 +1,5 @@
 #define OC_KT float
 #define OC_KNAME f32
-#define OC_MAX_HD 128
+#define OC_HEADDIM 16
 #define OC_VTYPES(X) X(0, float)
 #include "oc_inst.cuh"

@@ -61,7 +61,7 @@ extern "C" int oc_fused_attention_v2_noalloc(const void* q, int q_dtype, int64_t
   int splits = num_splits > 0 ? num_splits : oc_auto_num_splits(tiles, sms);
   if (tiles > 0 && splits > tiles) splits = (int)tiles;
   if (splits < 1) splits = 1;
-  const size_t need = oc_workspace_bytes(num_heads, 1, splits, head_dim);
+  const size_t need = oc_workspace_bytes(num_heads, 1, tiles, head_dim);
   if (need > kScratchBytes) return OC_ERR_TOO_LARGE;
   void* ws = nullptr;
   const int r = scratch_address(&ws);

@@ -92,7 +92,7 @@ def fused_orthocache_attention_v2(
 
     lib = _lib.load()
     ws = _lib.workspace(dev)
-    wbytes = lib.oc_workspace_bytes(num_heads, 1, num_splits, head_dim)
+    wbytes = lib.oc_workspace_bytes(num_heads, 1, num_tiles, head_dim)
     wbuf = ws.get(wbytes)
     if stats:
         ws.ctrl[0].zero_()
@@ -156,7 +156,7 @@ def fused_orthocache_attention(
     lib = _lib.load()
     ws = _lib.workspace(dev)
     splits = lib.oc_auto_num_splits(num_tiles, _lib.num_sms(dev))
-    wbuf = ws.get(lib.oc_workspace_bytes(1, 1, splits, head_dim))
+    wbuf = ws.get(lib.oc_workspace_bytes(1, 1, num_tiles, head_dim))
     if stats:
         ws.ctrl[0].zero_()
     _lib.check(lib.oc_fused_attention_v1(

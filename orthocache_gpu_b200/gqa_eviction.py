@@ -83,7 +83,7 @@ def fused_orthocache_attention_v3_gqa(
 
     lib = _lib.load()
     ws = _lib.workspace(dev)
-    wbuf = ws.get(lib.oc_workspace_bytes(num_seqs * num_kv_heads, G, num_splits, head_dim))
+    wbuf = ws.get(lib.oc_workspace_bytes(num_seqs * num_kv_heads, G, num_tiles, head_dim))
     if stats:
         ws.ctrl[0].zero_()
     _lib.check(lib.oc_fused_attention_v3_gqa(

@@ -94,7 +94,7 @@ def fused_orthocache_attention_paged(
 
     lib = _lib.load()
     ws = _lib.workspace(dev)
-    wbuf = ws.get(lib.oc_workspace_bytes(num_seqs * num_kv_heads, group, num_splits, head_dim))
+    wbuf = ws.get(lib.oc_workspace_bytes(num_seqs * num_kv_heads, group, num_tiles, head_dim))
     if stats:
         ws.ctrl[0].zero_()
     gate = _lib.OC_GATE_ZETA if tau is None else _lib.OC_GATE_CAUCHY_SCHWARZ

@@ -44,7 +44,7 @@ def test_noalloc_entry_point_matches_workspace_entry_point():
         cref = torch.zeros(2, dtype=torch.int32, device=dev)
         cgot = torch.zeros(2, dtype=torch.int32, device=dev)
         splits = lib.oc_auto_num_splits(tiles, torch.cuda.get_device_properties(dev).multi_processor_count)
-        ws = torch.zeros(lib.oc_workspace_bytes(heads, 1, splits, 128), dtype=torch.uint8, device=dev)
+        ws = torch.zeros(lib.oc_workspace_bytes(heads, 1, tiles, 128), dtype=torch.uint8, device=dev)
         assert _call(lib, lib.oc_fused_attention_v2, q, k, v, ref, mref, cref, 1.0,
                      (ws.data_ptr(), ws.numel())) == 0
         assert _call(lib, lib.oc_fused_attention_v2_noalloc, q, k, v, got, mgot, cgot, 1.0, ()) == 0
