@@ -57,20 +57,24 @@ bool types_supported(int q_dtype, int k_dtype, int v_dtype, int out_dtype) {
 
 int run(const DecodeParams& p, int k_dtype, int v_dtype, int hd, bool attn, int sms, cudaStream_t st) {
   const int gc = gc_for_group(p.group);
+  // tensor cores need 16-bit keys, values of the same type and, for attention,
+  // queries of that type too (the logits are then exact products in fp32)
+  const bool tc = (k_dtype == OC_F16 || k_dtype == OC_BF16) && v_dtype == k_dtype && hd >= 64 &&
+                  (!attn || p.q_dtype == k_dtype);
 #define OC_HDS(K, ...)                                              \
   switch (hd) {                                                     \
-    case 16: return oc::dispatch_##K##_16(p, v_dtype, gc, attn, sms, st);   \
-    case 32: return oc::dispatch_##K##_32(p, v_dtype, gc, attn, sms, st);   \
-    case 64: return oc::dispatch_##K##_64(p, v_dtype, gc, attn, sms, st);   \
-    case 128: return oc::dispatch_##K##_128(p, v_dtype, gc, attn, sms, st); \
+    case 16: return oc::dispatch_##K##_16(p, v_dtype, gc, attn, sms, st, tc);   \
+    case 32: return oc::dispatch_##K##_32(p, v_dtype, gc, attn, sms, st, tc);   \
+    case 64: return oc::dispatch_##K##_64(p, v_dtype, gc, attn, sms, st, tc);   \
+    case 128: return oc::dispatch_##K##_128(p, v_dtype, gc, attn, sms, st, tc); \
     __VA_ARGS__                                                     \
     default: return OC_ERR_UNSUPPORTED;                             \
   }
   switch (k_dtype) {
     case OC_F32: OC_HDS(f32)
-    case OC_F16: OC_HDS(f16, case 256: return oc::dispatch_f16_256(p, v_dtype, gc, attn, sms, st);)
-    case OC_BF16: OC_HDS(bf16, case 256: return oc::dispatch_bf16_256(p, v_dtype, gc, attn, sms, st);)
-    case OC_F8E4M3: OC_HDS(f8, case 256: return oc::dispatch_f8_256(p, v_dtype, gc, attn, sms, st);)
+    case OC_F16: OC_HDS(f16, case 256: return oc::dispatch_f16_256(p, v_dtype, gc, attn, sms, st, tc);)
+    case OC_BF16: OC_HDS(bf16, case 256: return oc::dispatch_bf16_256(p, v_dtype, gc, attn, sms, st, tc);)
+    case OC_F8E4M3: OC_HDS(f8, case 256: return oc::dispatch_f8_256(p, v_dtype, gc, attn, sms, st, tc);)
     default: return OC_ERR_UNSUPPORTED;
   }
 #undef OC_HDS

@@ -32,15 +32,15 @@ OC_HD int64_t range_owner(int64_t r, int64_t n, int64_t W) { return ((r + 1) * W
 
 // Tile index of the k-th tile (split-major order) of a unit with T tiles and
 // S splits: split s holds tiles s, s+S, ...; splits s < T%S hold one more.
-OC_HD int64_t split_major_tile(int64_t k, int64_t T, int64_t S) {
+OC_HD int split_major_tile(int k, int T, int S) {
   if (S <= 1 || T <= 0) return k;
-  const int64_t q = T / S, r = T % S;
-  int64_t s, j;
+  const int q = T / S, r = T % S;
+  int s, j;
   if (k < r * (q + 1)) {
     s = k / (q + 1);
     j = k % (q + 1);
   } else {
-    const int64_t k2 = k - r * (q + 1);
+    const int k2 = k - r * (q + 1);
     s = r + k2 / q;
     j = k2 % q;
   }
