@@ -27,9 +27,8 @@
  * Thresholds are given in double precision and compared exactly as the
  * reference's CPU path compares them (see the notes at each function).
  *
- * Workspace: a fixed header (grid-barrier counters, per-unit counts and merge
- * tickets) followed by per-call scratch (retained-tile list, their logits,
- * split partial states).  Size it with oc_workspace_bytes(); it must be
+ * Workspace: a fixed header (merge tickets) followed by the split partial
+ * states; its size depends only on the query group and head_dim.  Size it with oc_workspace_bytes(); it must be
  * zero-filled once before first use and every launch leaves the header zeroed
  * again.  Launches that share a workspace must not overlap on the GPU.  A
  * non-zero *status word after a launch (OC_STATUS_*) means the outputs of that
@@ -169,10 +168,11 @@ int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_strid
  * inside another framework's allocator, under a memory budget, or from a
  * plugin interface that hands over only inputs and outputs.  Same arguments
  * and results as oc_fused_attention_v2 minus the workspace: the split-K
- * scratch lives in a 32 MiB array that this library reserves statically on
- * every GPU that loads it, held until the process exits.  A call whose
- * scratch would exceed 32 MiB returns OC_ERR_TOO_LARGE (roughly: heads *
- * tiles * 260 bytes + 1.4 MiB at head_dim 128).  It calls no cudaMalloc or
+ * scratch lives in a 2 MiB array that this library reserves statically on
+ * every GPU that loads it, held until the process exits.  The scratch does
+ * not grow with the number of heads or tokens (about 0.03 MiB + 10 KiB *
+ * (head_dim + 16)): head_dim up to 128 fits, and a call whose scratch would
+ * exceed 2 MiB (head_dim 256) returns OC_ERR_TOO_LARGE.  It calls no cudaMalloc or
  * cudaFree.  The first call on each device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make that first
  * call before any stream capture.  Every call zeroes the array's merge

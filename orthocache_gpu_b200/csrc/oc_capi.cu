@@ -5,6 +5,11 @@
 #include <cfloat>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
+#include <utility>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "../../include/orthocache_b200.h"
 #include "oc_decode.cuh"
@@ -55,26 +60,107 @@ bool types_supported(int q_dtype, int k_dtype, int v_dtype, int out_dtype) {
   return k_dtype == v_dtype;
 }
 
-int run(const DecodeParams& p, int k_dtype, int v_dtype, int hd, bool attn, int sms, cudaStream_t st) {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// TMA descriptor of the K or V tensor as a 4-D view {head_dim, token, kv
+// head, sequence-or-block} whose dimensions 1..3 are ordered by stride (the
+// copy engine wants increasing strides); pos[role] returns the dimension of
+// role 0 (token), 1 (kv head), 2 (sequence or block).  Box: one 64-column
+// panel with the 128-byte swizzle (tensor-core path) or a whole row, by
+// p.box_rows tokens.
+bool make_map(CUtensorMap* m, const char* base, int dtype, int hd, bool tc, const DecodeParams& p, bool isv,
+              int (&pos)[3]) {
+  const auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const int esz = elem_bytes(dtype);
+  int64_t size[3], stride[3];
+  size[0] = p.layout == oc::LAYOUT_LINEAR ? (int64_t)p.num_tiles * 64 : ((int64_t)1 << p.block_shift);
+  stride[0] = isv ? p.v_tok_stride : p.k_tok_stride;
+  size[1] = p.num_kv_heads;
+  stride[1] = isv ? p.v_head_stride : p.k_head_stride;
+  size[2] = p.layout == oc::LAYOUT_LINEAR ? p.num_seqs : p.num_blocks;
+  stride[2] = p.layout == oc::LAYOUT_LINEAR ? (isv ? p.v_seq_stride : p.k_seq_stride)
+                                            : (isv ? p.v_blk_stride : p.k_blk_stride);
+  // order the roles by stride; extent-1 roles go last with a stride that nests
+  int order[3] = {0, 1, 2};
+  auto key = [&](int r) { return size[r] == 1 ? INT64_MAX : stride[r]; };
+  for (int i = 0; i < 3; ++i)
+    for (int j = i + 1; j < 3; ++j)
+      if (key(order[j]) < key(order[i])) std::swap(order[i], order[j]);
+  cuuint64_t gdim[4], gstr[3];
+  gdim[0] = (cuuint64_t)hd;
+  int64_t last = (int64_t)hd * esz;
+  for (int i = 0; i < 3; ++i) {
+    const int r = order[i];
+    gdim[i + 1] = (cuuint64_t)size[r];
+    int64_t st = stride[r];
+    if (size[r] == 1 || st <= 0) st = (last + 15) / 16 * 16;
+    gstr[i] = (cuuint64_t)st;
+    last = st * size[r];
+    pos[r] = i + 1;
+  }
+  cuuint32_t box[4] = {(cuuint32_t)(tc ? 64 : hd), 1, 1, 1};
+  box[pos[0]] = (cuuint32_t)p.box_rows;
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUtensorMapDataType dt;
+  switch (dtype) {
+    case OC_F32: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; break;
+    case OC_F16: dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; break;
+    case OC_BF16: dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; break;
+    default: dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; break;
+  }
+  const CUresult r = enc(m, dt, 4, const_cast<char*>(base), gdim, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         tc ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int run(const DecodeParams& p0, int k_dtype, int v_dtype, int hd, bool attn, int sms, cudaStream_t st) {
+  DecodeParams p = p0;
   const int gc = gc_for_group(p.group);
+  p.box_rows = p.layout == oc::LAYOUT_LINEAR ? 64 : ((1 << p.block_shift) < 64 ? (1 << p.block_shift) : 64);
   // tensor cores need 16-bit keys, values of the same type and, for attention,
-  // queries of that type too (the logits are then exact products in fp32)
+  // queries of that type too (the logits are then exact products in fp32);
+  // swizzled boxes start on 1024-byte boundaries, so at least 8 rows a box
   const bool tc = (k_dtype == OC_F16 || k_dtype == OC_BF16) && v_dtype == k_dtype && hd >= 64 &&
-                  (!attn || p.q_dtype == k_dtype);
+                  (!attn || p.q_dtype == k_dtype) && p.box_rows >= 8;
+  // unswizzled boxes start on 128-byte boundaries
+  if (!tc && ((p.box_rows * hd * elem_bytes(k_dtype)) % 128 || (attn && (p.box_rows * hd * elem_bytes(v_dtype)) % 128)))
+    return OC_ERR_UNSUPPORTED;
+  oc::TensorMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  const bool any_tile = p.num_tiles > 0 && p.k != nullptr;
+  if (any_tile) {
+    if (!make_map(&maps.k, p.k, k_dtype, hd, tc, p, false, p.tm_pos_k)) return OC_ERR_INVALID;
+    if (attn && !make_map(&maps.v, p.v, v_dtype, hd, tc, p, true, p.tm_pos_v)) return OC_ERR_INVALID;
+  } else {
+    for (int i = 0; i < 3; ++i) p.tm_pos_k[i] = p.tm_pos_v[i] = i + 1;
+  }
 #define OC_HDS(K, ...)                                              \
   switch (hd) {                                                     \
-    case 16: return oc::dispatch_##K##_16(p, v_dtype, gc, attn, sms, st, tc);   \
-    case 32: return oc::dispatch_##K##_32(p, v_dtype, gc, attn, sms, st, tc);   \
-    case 64: return oc::dispatch_##K##_64(p, v_dtype, gc, attn, sms, st, tc);   \
-    case 128: return oc::dispatch_##K##_128(p, v_dtype, gc, attn, sms, st, tc); \
+    case 16: return oc::dispatch_##K##_16(p, maps, v_dtype, gc, attn, sms, st, tc);   \
+    case 32: return oc::dispatch_##K##_32(p, maps, v_dtype, gc, attn, sms, st, tc);   \
+    case 64: return oc::dispatch_##K##_64(p, maps, v_dtype, gc, attn, sms, st, tc);   \
+    case 128: return oc::dispatch_##K##_128(p, maps, v_dtype, gc, attn, sms, st, tc); \
     __VA_ARGS__                                                     \
     default: return OC_ERR_UNSUPPORTED;                             \
   }
   switch (k_dtype) {
     case OC_F32: OC_HDS(f32)
-    case OC_F16: OC_HDS(f16, case 256: return oc::dispatch_f16_256(p, v_dtype, gc, attn, sms, st, tc);)
-    case OC_BF16: OC_HDS(bf16, case 256: return oc::dispatch_bf16_256(p, v_dtype, gc, attn, sms, st, tc);)
-    case OC_F8E4M3: OC_HDS(f8, case 256: return oc::dispatch_f8_256(p, v_dtype, gc, attn, sms, st, tc);)
+    case OC_F16: OC_HDS(f16, case 256: return oc::dispatch_f16_256(p, maps, v_dtype, gc, attn, sms, st, tc);)
+    case OC_BF16: OC_HDS(bf16, case 256: return oc::dispatch_bf16_256(p, maps, v_dtype, gc, attn, sms, st, tc);)
+    case OC_F8E4M3: OC_HDS(f8, case 256: return oc::dispatch_f8_256(p, maps, v_dtype, gc, attn, sms, st, tc);)
     default: return OC_ERR_UNSUPPORTED;
   }
 #undef OC_HDS
@@ -89,31 +175,22 @@ int sms_or_device(int num_sms) {
 }
 
 // Workspace layout (every region 256-byte aligned):
-//   fixed header (kFixedBytes, zero between launches):
-//     [0, 256)             grid-barrier counters
-//     [256, +4*kMaxUnits)  retained tiles per unit
-//     [.., +4*kMaxUnits)   merge tickets per unit
-//   cnt_warp  kMaxWarps u32
-//   list      units*num_tiles i32
-//   part      2*kMaxWarps*gc*(hd+4) f32
-//   lg        units*num_tiles*gc*64 f32
+//   fixed header (kFixedBytes, zero between launches): merge tickets, one per
+//     (unit, 64-column panel), at most 4 panels a unit
+//   part  partial states, 2 slots per team of warps: 2*kMaxWarps*gc*(hd+16) f32
 constexpr int64_t kMaxUnits = 2048;  // units per launch (shared-memory prefix arrays)
 constexpr int64_t kMaxWarps = 1280;
 constexpr size_t pad256(size_t b) { return (b + 255) & ~size_t(255); }
-constexpr size_t kFixedBytes = pad256(256 + 2 * 4 * kMaxUnits);
+constexpr size_t kFixedBytes = pad256(4 * 4 * kMaxUnits);
 
 struct WsLayout {
-  size_t cnt_warp, list, part, lg, total;
+  size_t part, total;
 };
 
-WsLayout ws_layout(int64_t units, int gc, int64_t num_tiles, int hd) {
+WsLayout ws_layout(int64_t /*units*/, int gc, int64_t /*num_tiles*/, int hd) {
   WsLayout L;
-  const int64_t n = units * num_tiles;
-  L.cnt_warp = kFixedBytes;
-  L.list = L.cnt_warp + pad256(4 * kMaxWarps);
-  L.part = L.list + pad256(4 * (size_t)n);
-  L.lg = L.part + pad256(4 * (size_t)2 * kMaxWarps * gc * (hd + 4));
-  L.total = L.lg + pad256(4 * (size_t)n * gc * 64);
+  L.part = kFixedBytes;
+  L.total = L.part + pad256(4 * (size_t)2 * kMaxWarps * gc * (hd + 16));
   return L;
 }
 
@@ -122,13 +199,8 @@ int attach_workspace(DecodeParams& p, int64_t units, int hd, void* ws, size_t ws
   const WsLayout L = ws_layout(units, gc, p.num_tiles, hd);
   if (ws == nullptr || ws_bytes < L.total || !aligned16(ws)) return OC_ERR_WORKSPACE;
   char* b = static_cast<char*>(ws);
-  p.gbar = reinterpret_cast<uint32_t*>(b);
-  p.cnt_unit = reinterpret_cast<uint32_t*>(b + 256);
-  p.tickets = reinterpret_cast<uint32_t*>(b + 256 + 4 * kMaxUnits);
-  p.cnt_warp = reinterpret_cast<uint32_t*>(b + L.cnt_warp);
-  p.list = reinterpret_cast<int32_t*>(b + L.list);
+  p.tickets = reinterpret_cast<uint32_t*>(b);
   p.part = reinterpret_cast<float*>(b + L.part);
-  p.lg = reinterpret_cast<float*>(b + L.lg);
   return OC_OK;
 }
 
@@ -156,7 +228,7 @@ const char* oc_status_string(int code) {
     case OC_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
     case OC_ERR_CUDA: return "CUDA launch failed";
     case OC_ERR_TOO_LARGE:
-      return "problem needs more scratch than the fixed 32 MiB of oc_fused_attention_v2_noalloc";
+      return "problem needs more scratch than the fixed 2 MiB of oc_fused_attention_v2_noalloc";
     default: return "unknown status";
   }
 }

@@ -7,23 +7,23 @@
 //   * paged KV (block-table gather) ............ paged_eviction.py:56-237
 //   * mask / zeta scoring only ................. fwht_fused_prototype.py:102-192
 //
-// Design: a persistent cooperative kernel, one CTA per SM; every warp is an
-// independent decoder with its own double-buffered shared-memory ring fed by
-// the bulk-copy (TMA) engine, so the per-tile path has no CTA-wide barrier.
+// Design: one persistent CTA per SM, every warp an independent decoder with
+// its own shared-memory ring of tile slots (16-byte cp.async copies, one
+// commit group per slot, consumed in order), so the per-tile path has no
+// CTA-wide or grid-wide barrier.
 //
-//   Phase A (K stream).  The tiles of all units (sequence, kv head, query
-//   chunk) are flattened (oc_plan.h) and split into equal contiguous ranges,
-//   one per warp.  A warp scores each 64-token K tile; for a retained tile it
-//   computes the query logits and stores them (fp32, log2 domain) with the
-//   tile's flattened index in scratch.  An evicted tile costs one K read.
-//   Grid barrier (bounded spin; the launch is cooperative, all CTAs resident).
-//   Phase B (V stream).  The Kt retained tiles, in flattened order, are split
-//   into equal rank ranges over min(W, Kt) warps, so V traffic is balanced
-//   whatever the eviction pattern.  A warp streams V (with the stored logits)
-//   of its tiles and keeps an online-softmax state per unit; a unit touched by
-//   several warps is merged (log-sum-exp) by the last of them to finish
-//   (atomic ticket), so one launch gives the final output.  V of an evicted
-//   tile is never read.
+//   The tiles of all units (sequence, kv head, query chunk) are flattened
+//   (oc_plan.h) and split into equal contiguous ranges, one per warp; inside a
+//   unit the order is the reference's interleaved split order, so a range
+//   samples the whole sequence and retained work evens out across warps.  A
+//   warp scores each 64-token K tile; for a retained tile it computes the
+//   query logits (fp32, log2 domain) into the slot's logit area and reuses the
+//   slot for the tile's V, which is consumed after the copies already in
+//   flight.  An evicted tile costs one K read; its V is never read.  A unit's
+//   online-softmax state is written once its K tiles in the range are gated
+//   and no V copy of it is pending: directly when the range holds the whole
+//   unit, else as a partial state that the last of the unit's warps merges
+//   (log-sum-exp, atomic ticket), so one launch gives the final output.
 //
 // Band energies use closed forms of the natural-order 64-point Walsh
 // transform along the token axis of the tile (no 64x64 matmul):
@@ -44,6 +44,8 @@
 // kernel carries on to completion (the outputs of that launch are invalid).
 #pragma once
 
+#include <cuda.h>
+#include <cstdio>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
@@ -84,11 +86,6 @@ constexpr int kMaxWarpsPerCta = OC_MAX_WARPS_PER_CTA;
 #define OC_COPY_SPLIT 1
 #endif
 constexpr int kCopySplit = OC_COPY_SPLIT;
-#ifdef OC_PROBE_NO_GATE_MATH
-constexpr bool kGateMath = false;  // measurement probe: stream tiles, skip the band energies
-#else
-constexpr bool kGateMath = true;
-#endif
 constexpr int kUnrollPV = OC_UNROLL_PV;
 
 struct DecodeParams {
@@ -109,6 +106,8 @@ struct DecodeParams {
   int block_shift, num_blocks;
   const int32_t* seq_lens;  // nullable: every sequence has num_tiles*64 tokens
   int layout;
+  int box_rows;  // tokens per TMA box: 64, or the page size when pages are smaller
+  int tm_pos_k[3], tm_pos_v[3];  // tensor-map dimension of the token / kv-head / outer index
   int num_seqs, num_kv_heads, group, num_tiles, num_splits;
   int gate;
   float thr;
@@ -120,14 +119,9 @@ struct DecodeParams {
   float* score;       // same shape: zeta or Cauchy-Schwarz bound, nullable
   uint32_t* stats;    // [0] += retained tiles, nullable
   uint32_t* status;   // error bits, non-null
-  // workspace (attention only); gbar, cnt_unit and tickets are zero between launches
-  uint32_t* gbar;      // [2] grid-barrier arrive / depart counters
-  uint32_t* cnt_unit;  // retained tiles per unit (phase A atomics)
-  uint32_t* tickets;   // merge tickets per unit
-  uint32_t* cnt_warp;  // retained tiles per phase-A warp
-  int32_t* list;       // flattened index of each retained tile, at its phase-A position
-  float* lg;           // logits of each retained tile at that position: [g][rg][m], GC*64 floats
-  float* part;         // partial states [2*W][GC][HD + 4]: acc[HD], m, l
+  // workspace (attention only); tickets are zero between launches
+  uint32_t* tickets;   // merge tickets per (unit, panel)
+  float* part;         // partial states [2 * teams][GC][P][HD/P + 4]: acc, m, l
   // shard mode (nullable): write the merged partial state (m, l, unnormalised
   // acc) of each query head instead of the normalised output
   float* sh_m;
@@ -231,6 +225,14 @@ __device__ __forceinline__ float warp_sum(float x) {
   for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
   return x;
 }
+__device__ __forceinline__ float2 warp_sum2(float2 x) {  // two independent butterflies
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    x.x += __shfl_xor_sync(0xffffffffu, x.x, o);
+    x.y += __shfl_xor_sync(0xffffffffu, x.y, o);
+  }
+  return x;
+}
 __device__ __forceinline__ float warp_max(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
@@ -263,14 +265,8 @@ __device__ __forceinline__ void reduce_scatter(float* v, int c) {
 
 __device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
 
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // ---------------------------------------------------------------- config
-template <typename KT, typename VT, int HD, int GC, bool ATTN, int NSLOT>
+template <typename KT, typename VT, int HD, int GC, bool ATTN, int NSLOT, bool TC>
 struct Cfg {
   static constexpr int KB = Elem<KT>::B;
   static constexpr int VB = Elem<VT>::B;
@@ -287,49 +283,51 @@ struct Cfg {
   static constexpr int VCB = DPT * VB;   // bytes of a V row per lane
   static constexpr int ROWMAX = (ATTN && ROWV > ROWK) ? ROWV : ROWK;
   static constexpr int LGB = ATTN ? GC * 64 * 4 : 0;
-  static constexpr int SLOT = (64 * ROWMAX + LGB + 127) / 128 * 128;
-  static constexpr int RING = 200 * 1024;
-  static constexpr int NW0 = RING / (NSLOT * SLOT);
+  // Tensor-core path: a team of P = HD/64 warps shares each tile, one
+  // 64-column panel (HDL columns) per warp; otherwise P = 1.
+  static constexpr int P = TC ? HD / 64 : 1;
+  static constexpr int HDL = HD / P;
+  static constexpr int SLOT = 64 * ROWMAX / P;  // a multiple of 1024: 128-byte swizzle atoms stay aligned
+  static constexpr int RING = 208 * 1024;
+  static constexpr int NW0 = RING / (NSLOT * (SLOT + LGB));
   static constexpr int NWC = NW0 > kMaxWarpsPerCta ? kMaxWarpsPerCta : NW0;
-  static constexpr int NW = NWC < 1 ? 1 : NWC;
+  static constexpr int NW = NWC < P ? P : NWC / P * P;  // whole teams
   static constexpr int NT = NW * 32;
   static constexpr int MAXU = 2048;  // units per launch (the host batches larger problems)
   static constexpr int MAXW = 1280;  // warps per grid
-  static constexpr int OFF_BAR = NW * NSLOT * SLOT;
-  static constexpr int OFF_TP = OFF_BAR;
-  static constexpr int OFF_KP = OFF_TP + 4 * (MAXU + 1);
-  static constexpr int OFF_PA = OFF_KP + (ATTN ? 4 * (MAXU + 1) : 0);
-  static constexpr int OFF_MISC = OFF_PA + (ATTN ? 4 * (MAXW + 1) : 0);
-  static constexpr int SMEM = (OFF_MISC + 64 + 127) / 128 * 128;
+  static constexpr int OFF_LGS = NW * NSLOT * SLOT;         // logits of slot s: [NW][NSLOT][GC*64] floats
+  static constexpr int OFF_BAR = OFF_LGS + NW * NSLOT * LGB;  // full barrier of each slot
+  static constexpr int OFF_XCH = OFF_BAR + 8 * NW * NSLOT;    // band energies exchanged in a team: [NW/P][2][P] float2
+  static constexpr int OFF_TP = OFF_XCH + 16 * NW;
+  static constexpr int OFF_MISC = OFF_TP + 4 * (MAXU + 1);
+  static constexpr int SMEM = (OFF_MISC + 4 * 32 + 127) / 128 * 128 + 1024;  // + base alignment slack
   static_assert(C >= 1 && C <= 32 && (C & (C - 1)) == 0, "K row bytes must be a power of two in 16..512");
   static_assert(D2 >= 2 && (VCB % 16) == 0, "vector widths");
-  static_assert(NW * NSLOT * SLOT >= 4 * NT, "ring doubles as scan scratch");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-// Block-wide inclusive scan of a[1..n] in place, a[0] = 0; tmp holds blockDim.x ints.
+// Block-wide inclusive scan of a[1..n] in place, a[0] = 0; tmp holds one int per warp.
+// Each thread scans a contiguous chunk; chunk totals are scanned with warp shuffles.
 __device__ __noinline__ static void block_scan(int* a, int n, int* tmp) {
   __syncthreads();
-  const int nt = blockDim.x, tid = threadIdx.x;
+  const int nt = blockDim.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int per = (n + nt - 1) / nt;
   const int lo = 1 + tid * per, hi = min(n + 1, lo + per);
   int run = 0;
   for (int i = lo; i < hi; ++i) run += a[i];
-  tmp[tid] = run;
-  __syncthreads();
-  if (tid == 0) {
-    int acc = 0;
-    for (int t = 0; t < nt; ++t) {
-      const int x = tmp[t];
-      tmp[t] = acc;
-      acc += x;
-    }
+  int inc = run;  // inclusive scan of the chunk totals inside the warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
   }
+  if (lane == 31) tmp[wid] = inc;
   __syncthreads();
-  run = tmp[tid];
+  int base = inc - run;
+  for (int w = 0; w < wid; ++w) base += tmp[w];
   for (int i = lo; i < hi; ++i) {
-    run += a[i];
-    a[i] = run;
+    base += a[i];
+    a[i] = base;
   }
   if (tid == 0) a[0] = 0;
   __syncthreads();
@@ -350,30 +348,43 @@ __device__ __forceinline__ int upper_index(const int* a, int n, int64_t x) {
 // logits and PV on the tensor cores (mma.sync m16n8k16), tiles stored
 // swizzled in shared memory.  Otherwise the same math runs on CUDA cores.
 template <typename KT, typename VT, int HD, int GC, bool ATTN, int NSLOT, bool TC>
-__global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
-    decode_kernel(const DecodeParams p) {
-  using CF = Cfg<KT, VT, HD, GC, ATTN, NSLOT>;
+__global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
+    decode_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV) {
+  using CF = Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>;
   constexpr int C = CF::C, RG = CF::RG, RPL = CF::RPL, PAIRS = CF::PAIRS, DPT = CF::DPT, D2 = CF::D2;
   constexpr int RGE = CF::RGE, NRES = CF::NRES, NW = CF::NW, SLOT = CF::SLOT;
-  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int P = CF::P, HDL = CF::HDL;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  // 1024-byte aligned base: the TMA 128-byte swizzle repeats every 1024 bytes
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c = lane % C, rg = lane / C;
   static_assert(!TC || (CF::KB == 2 && CF::VB == 2 && HD >= 64 && GC <= 8), "tensor-core path");
   constexpr bool KBF16 = TC && (sizeof(KT) == 2) && !std::is_same<KT, __half>::value;
   const int g8 = lane >> 2, t4 = lane & 3;  // mma fragment coordinates
-  const int64_t W = (int64_t)gridDim.x * NW;
-  const int64_t wg = (int64_t)blockIdx.x * NW + warp;
+  // team of P warps (one 64-column panel each on the tensor-core path); work is assigned per team
+  const int team = warp / P, panel = warp % P;
+  const int64_t W = (int64_t)gridDim.x * (NW / P);        // teams in the grid
+  const int64_t wg = (int64_t)blockIdx.x * (NW / P) + team;  // this warp's team
+  auto team_sync = [&]() {
+    if constexpr (P > 1) asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "r"(32 * P) : "memory");
+  };
   const int nchunks = (p.group + GC - 1) / GC;
   const int U = p.num_seqs * p.num_kv_heads * nchunks;
   const int S = p.num_splits;
 
   int* tp = reinterpret_cast<int*>(smem + CF::OFF_TP);
-  int* kp = reinterpret_cast<int*>(smem + CF::OFF_KP);
-  int* pa = reinterpret_cast<int*>(smem + CF::OFF_PA);
-  int* misc = reinterpret_cast<int*>(smem + CF::OFF_MISC);
-  int* scan_tmp = reinterpret_cast<int*>(smem);  // the ring, while no copy is in flight
+  int* scan_tmp = reinterpret_cast<int*>(smem + CF::OFF_MISC);
   unsigned char* ring = smem + warp * NSLOT * SLOT;
+  float* lgs_all = reinterpret_cast<float*>(smem + CF::OFF_LGS);  // [NW][NSLOT][GC*64]
+  float* lgs_base = lgs_all + warp * NSLOT * (CF::LGB / 4);
+  float2* xch = reinterpret_cast<float2*>(smem + CF::OFF_XCH) + team * 2 * P;
+  const uint32_t bar0 = smem_u32(smem + CF::OFF_BAR) + 8u * warp * NSLOT;  // this warp's slot barriers
+  if (lane < NSLOT) mbar_init(bar0 + 8u * lane, 1);
+  mbar_init_fence();
+  __syncwarp();
 
   // ---- tiles per unit, prefix in shared memory
   for (int u = tid; u < U; u += blockDim.x) {
@@ -390,217 +401,425 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
   const int64_t N = tp[U];
 
   const uint64_t pol = policy_evict_first();
-  uint32_t item = 0;  // tiles this warp has consumed, across both phases
 
   auto unit_seq = [&](int u) { return u / (p.num_kv_heads * nchunks); };
   auto unit_kvh = [&](int u) { return (u / nchunks) % p.num_kv_heads; };
   auto unit_chunk = [&](int u) { return u % nchunks; };
   auto tile_of = [&](int u, int64_t f) { return split_major_tile((int)(f - tp[u]), tp[u + 1] - tp[u], S); };
 
-  // Bulk copy of tile `tile` of unit u (K or V) into ring slot s, plus
-  // `extra_bytes` from `extra` (the stored logits) after the tile.
-  // Byte offset of tile byte o (row-major, `row` bytes per row) in shared
-  // memory: on the tensor-core path the 16-byte chunks of each row are XORed
-  // with (row & 7), so ldmatrix reads of 8 rows hit 8 distinct bank groups.
-  auto swz = [&](int o, int r) -> int {
-    if constexpr (TC) {
-      return o ^ ((r & 7) << 4);
-    } else {
-      return o;
+  // smem address of (token, dim) of a 16-bit tile on the tensor-core path:
+  // 64-column panels of 64 tokens x 128 bytes, the 16-byte chunks of a row
+  // XORed with (token & 7) by the TMA 128-byte swizzle, so ldmatrix reads of
+  // 8 rows hit 8 distinct bank groups.
+  //   tc_addr(tok, dim) = base + tok * 128 + ((((dim * 2) >> 4) ^ (tok & 7)) << 4)  (dim < 64)
+  // Per-lane parts of the ldmatrix addresses (x = lane & 7, b3 / b4 = lane bits 3 / 4):
+  // every row a lane addresses has (row & 7) == x, so the swizzled chunk of
+  // column 16 c + 8 b is ((2 c + b) ^ x).
+  uint32_t ch3[TC ? HDL / 16 : 1], ch4[TC ? HDL / 16 : 1];
+  uint32_t offG = 0, offL = 0, offV = 0;
+  if constexpr (TC) {
+    const uint32_t x = lane & 7, b3 = (lane >> 3) & 1, b4 = (lane >> 4) & 1;
+#pragma unroll
+    for (int c2 = 0; c2 < HDL / 16; ++c2) {
+      ch3[c2] = ((2u * c2 + b3) ^ x) << 4;
+      ch4[c2] = ((2u * c2 + b4) ^ x) << 4;
     }
-  };
-  // row of tile byte o (row sizes are compile-time powers of two)
-  auto row_of = [&](int o, bool isv) -> int { return isv ? o / CF::ROWV : o / CF::ROWK; };
-  // smem address of (token, dim) of a 16-bit tile with `row` bytes per row
-  auto tc_addr = [&](uint32_t base, int tok, int dim, int row) -> uint32_t {
-    return base + tok * row + ((((dim * 2) >> 4) ^ (tok & 7)) << 4);
-  };
+    offG = (x + 32u * b4) * 128u;  // gate: tokens 8 s4 + x (+32), columns 16 np + 8 b3
+    offL = (x + 8u * b3) * 128u;   // logits: tokens 16 mt + x + 8 b3, columns 16 ks + 8 b4
+    offV = (x + 8u * b4) * 128u;   // P V: tokens 16 ks + x + 8 b4, columns 16 mt + 8 b3
+  }
 
-  // Asynchronous copy (16-byte cp.async per lane, one commit group per item)
-  // of tile `tile` of unit u (K or V) into ring slot s, plus `extra_bytes`
-  // from `extra` (the stored logits) after the tile.  The warp's groups
-  // complete in order, so waiting for "at most NSLOT-1 pending" makes the
-  // oldest item resident.
-  auto issue = [&](uint32_t s, int u, int tile, bool isv, const float* extra, int extra_bytes) {
-#ifdef OC_PROBE_NO_LOAD
-    cp_async_commit();  // measurement probe: no memory traffic, the slot keeps stale data
-    return;
-#endif
+  // TMA copy of tile `tile` of unit u (K or V) into ring slot s: one box per
+  // page run (of this warp's 64-column panel on the tensor-core path), all
+  // completing on the slot's barrier.
+  // The slot was only read (generic proxy) since its last copy, so the next
+  // copy needs no proxy fence: __syncwarp orders the lanes' reads before it.
+  auto issue = [&](uint32_t s, int seq, int kvh, int tile, bool isv) {
+    const uint32_t fbar = bar0 + 8u * s;
     const uint32_t dst = smem_u32(ring + s * SLOT);
     const int row = isv ? CF::ROWV : CF::ROWK;
-    const int tbytes = 64 * row;
-    const int seq = unit_seq(u), kvh = unit_kvh(u);
-    const char* basep = isv ? p.v : p.k;
-    const int64_t tok = isv ? p.v_tok_stride : p.k_tok_stride;
-    if (p.layout == LAYOUT_LINEAR) {
-      const char* base = basep + (int64_t)seq * (isv ? p.v_seq_stride : p.k_seq_stride) +
-                         (int64_t)kvh * (isv ? p.v_head_stride : p.k_head_stride) + (int64_t)tile * 64 * tok;
-      if (tok == row) {
-#pragma unroll 8
-        for (int o = lane * 16; o < tbytes; o += 512) cp_async16(dst + swz(o, row_of(o, isv)), base + o, pol);
-      } else {
-#pragma unroll 8
-        for (int o = lane * 16; o < tbytes; o += 512) {
-          const int r = row_of(o, isv), col = o - r * row;
-          cp_async16(dst + swz(o, r), base + (int64_t)r * tok + col, pol);
-        }
+    const void* tm = isv ? static_cast<const void*>(&tmV) : static_cast<const void*>(&tmK);
+    const int* tpos = isv ? p.tm_pos_v : p.tm_pos_k;
+    __syncwarp();
+    if (p.layout == LAYOUT_LINEAR) {  // one box of 64 rows
+      if (lane == 0) {
+        mbar_arrive_expect_tx(fbar, 64u * row / P);
+        int cc[4];
+        cc[0] = panel * 64;
+        cc[tpos[0]] = tile * 64;
+        cc[tpos[1]] = kvh;
+        cc[tpos[2]] = seq;
+        tma_load_4d(dst, tm, cc[0], cc[1], cc[2], cc[3], fbar, pol);
       }
-    } else {
-      const int shift = p.block_shift;
-      const int64_t blk_stride = isv ? p.v_blk_stride : p.k_blk_stride;
-      const char* base = basep + (int64_t)kvh * (isv ? p.v_head_stride : p.k_head_stride);
-      const int32_t* bt = p.block_tables + (int64_t)seq * p.bt_seq_stride;
-      const int t0 = tile * 64;
-      const int first = t0 >> shift;
-      const int npages = ((t0 + 63) >> shift) - first + 1;
-      int mine = 0;  // physical block of page (first + lane)
-      if (lane < npages && npages <= 32) {
-        mine = bt[first + lane];
-        if (mine < 0 || mine >= p.num_blocks) {
-          atomicOr(p.status, ST_BAD_PAGE);
-          mine = 0;
-        }
-      }
-      const int bmask = (1 << shift) - 1;
-#pragma unroll 4
-      for (int o = lane * 16; o < tbytes; o += 512) {
-        const int r = row_of(o, isv), col = o - r * row;
-        const int t = t0 + r;
-        int pb;
-        if (npages <= 32) {
-          pb = __shfl_sync(0xffffffffu, mine, (t >> shift) - first);
-        } else {
-          pb = bt[t >> shift];
-          if (pb < 0 || pb >= p.num_blocks) {
-            atomicOr(p.status, ST_BAD_PAGE);
-            pb = 0;
-          }
-        }
-        cp_async16(dst + swz(o, r), base + (int64_t)pb * blk_stride + (int64_t)(t & bmask) * tok + col, pol);
-      }
+      return;
     }
-    for (int o = lane * 16; o < extra_bytes; o += 512)
-      cp_async16(dst + 64 * CF::ROWMAX + o, reinterpret_cast<const char*>(extra) + o, pol);
-    cp_async_commit();
+    if (lane == 0) mbar_arrive_expect_tx(fbar, 64u * row / P);
+    __syncwarp();
+    const int RB = p.box_rows;
+    const int nruns = 64 / RB;
+    for (int run = lane; run < nruns; run += 32) {
+      const int t = tile * 64 + run * RB;
+      int pb = p.block_tables[(int64_t)seq * p.bt_seq_stride + (t >> p.block_shift)];
+      if (pb < 0 || pb >= p.num_blocks) {
+        atomicOr(p.status, ST_BAD_PAGE);
+        pb = 0;
+      }
+      int cc[4];
+      cc[0] = panel * 64;
+      cc[tpos[0]] = t & ((1 << p.block_shift) - 1);
+      cc[tpos[1]] = kvh;
+      cc[tpos[2]] = pb;
+      tma_load_4d(dst + (uint32_t)(run * RB * (row / P)), tm, cc[0], cc[1], cc[2], cc[3], fbar, pol);
+    }
   };
 
-  auto wait_item = [&](uint32_t it) {
-    cp_async_wait<NSLOT - 1>();
+  // Wait for the copy in slot s (bounded; a timeout sets the status bit).
+  uint32_t phases = 0;  // bit s: parity of slot s's next completion
+#ifdef OC_PROBE_WAIT
+  long long pw_wait = 0, pw_t0 = clock64(), pw_gate = 0, pw_iss = 0;
+  int pw_n = 0;
+#endif
+  auto wait_slot = [&](uint32_t s) {
+#ifdef OC_PROBE_WAIT
+    const long long a0 = clock64();
+#endif
+    if (!mbar_wait_bounded(bar0 + 8u * s, (phases >> s) & 1u, kWaitLimit) && lane == 0)
+      atomicOr(p.status, ST_TIMEOUT);
+    phases ^= 1u << s;
+#ifdef OC_PROBE_WAIT
+    pw_wait += clock64() - a0;
+    ++pw_n;
+#endif
     __syncwarp();
-    return ring + (it % NSLOT) * SLOT;
+    return ring + s * SLOT;
   };
 
   float qmax = 0.f;  // max_g |q_g| of the current unit (Cauchy-Schwarz gate)
-  // ---- tensor-core constants: A fragments of W rows 1..7 (E_low) and of +-I (K[t] - K[t+32])
-  uint32_t aW[TC ? 4 : 1][4], aPos[4], aNeg[4];
+  uint32_t ktiles = 0;  // K tiles gated (selects the team's exchange buffer)
+  // ---- tensor-core gate constants.  The gate runs with the K tile as the A
+  // operand (A = K^T: 16 head-dim columns x 16 tokens) and a constant B:
+  // each k-step takes tokens {t0..t0+7} and {t0+32..t0+39}, so
+  //   B_low[k][n]  = W[n+1][k & 7]      (rows 1..7 of the 64-point natural-order
+  //                                      Walsh matrix depend only on token bits 0..2)
+  //   B_diff[k][n] = +1 if k == n, -1 if k == n + 8
+  // give, per k-step, 16 columns x (W K)_{1..7} partial sums and the 8
+  // differences K[t0+n] - K[t0+32+n].  Four k-steps (t0 = 0, 8, 16, 24) cover
+  // the tile: 8 MMAs per 16 columns.
+  uint32_t bLow = 0u, bDiff = 0u, bNeg = 0u;
   if constexpr (TC) {
-    const uint32_t P8 = KBF16 ? 0x3E00u : 0x3000u, N8 = KBF16 ? 0xBE00u : 0xB000u;
+    const uint32_t P8 = KBF16 ? 0x3E00u : 0x3000u, N8 = KBF16 ? 0xBE00u : 0xB000u;  // +-1/8
     const uint32_t ONE = KBF16 ? 0x3F80u : 0x3C00u, MONE = KBF16 ? 0xBF80u : 0xBC00u;
     auto w = [&](int r, int tk) -> uint32_t {
       if (r < 1 || r > 7) return 0u;  // row 0 (DC) and rows >= 8 do not enter E_low
       return (__popc(r & tk) & 1) ? N8 : P8;
     };
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      const int c0 = 16 * ks + 2 * t4;
-      aW[ks][0] = w(g8, c0) | (w(g8, c0 + 1) << 16);
-      aW[ks][1] = 0u;
-      aW[ks][2] = w(g8, c0 + 8) | (w(g8, c0 + 9) << 16);
-      aW[ks][3] = 0u;
-    }
-    const uint32_t ip = (g8 == 2 * t4 ? ONE : 0u) | ((g8 == 2 * t4 + 1 ? ONE : 0u) << 16);
-    const uint32_t in = (g8 == 2 * t4 ? MONE : 0u) | ((g8 == 2 * t4 + 1 ? MONE : 0u) << 16);
-    aPos[0] = ip; aPos[1] = 0u; aPos[2] = 0u; aPos[3] = ip;
-    aNeg[0] = in; aNeg[1] = 0u; aNeg[2] = 0u; aNeg[3] = in;
+    // B fragment: this lane holds B[2t4][g8], B[2t4+1][g8] (register 0) and rows +8 (register 1)
+    bLow = w(g8 + 1, 2 * t4) | (w(g8 + 1, 2 * t4 + 1) << 16);  // same for rows k+8 (same low bits)
+    bDiff = (g8 == 2 * t4 ? ONE : 0u) | ((g8 == 2 * t4 + 1 ? ONE : 0u) << 16);
+    bNeg = (g8 == 2 * t4 ? MONE : 0u) | ((g8 == 2 * t4 + 1 ? MONE : 0u) << 16);
   }
-  // E_low = sum (W K)[1..7]^2 and E_high = 1/2 sum (K[t]-K[t+32])^2 with mma:
-  // B = the K tile (tokens x head_dim), 16 columns per step.
+  // E_low = sum (W K)[1..7]^2 and E_high = 1/2 sum (K[t]-K[t+32])^2
   auto tc_gate = [&](const unsigned char* ts) -> float {
     const uint32_t base = smem_u32(ts);
-    float2 el2 = make_float2(0.f, 0.f), eh2 = make_float2(0.f, 0.f);
-#pragma unroll 2
-    for (int np = 0; np < HD / 16; ++np) {
-      float cl[2][4] = {}, cd[2][2][4] = {};
+    const bool need_low = (p.gate != GATE_CS);
+    float2 el2 = make_float2(0.f, 0.f), eh2 = make_float2(0.f, 0.f), eh3 = make_float2(0.f, 0.f);
+#pragma unroll 4
+    for (int np = 0; np < HDL / 16; ++np) {
+      float cl[4] = {}, cd[4][4] = {};
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        uint32_t b[4];
-        ldsm_x4_t(tc_addr(base, 16 * ks + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * np + ((lane >> 4) & 1) * 8,
-                          CF::ROWK), b);
-        mma16816<KBF16>(cl[0], aW[ks], b[0], b[1]);
-        mma16816<KBF16>(cl[1], aW[ks], b[2], b[3]);
-        mma16816<KBF16>(cd[ks & 1][0], ks < 2 ? aPos : aNeg, b[0], b[1]);
-        mma16816<KBF16>(cd[ks & 1][1], ks < 2 ? aPos : aNeg, b[2], b[3]);
+      for (int s4 = 0; s4 < 4; ++s4) {
+        uint32_t a[4];
+        ldsm_x4_t(base + offG + s4 * 1024 + ch3[np], a);  // tc_addr(8 s4 + x + 32 b4, 16 np + 8 b3)
+        if (need_low) mma16816<KBF16>(cl, a, bLow, bLow);
+        mma16816<KBF16>(cd[s4], a, bDiff, bNeg);
       }
+      el2 = __ffma2_rn(make_float2(cl[0], cl[1]), make_float2(cl[0], cl[1]), el2);
+      el2 = __ffma2_rn(make_float2(cl[2], cl[3]), make_float2(cl[2], cl[3]), el2);
 #pragma unroll
-      for (int n = 0; n < 2; ++n) {
-        const float2 x = make_float2(cl[n][0], cl[n][1]);
-        el2 = __ffma2_rn(x, x, el2);
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          const float2 y0 = make_float2(cd[mt][n][0], cd[mt][n][1]);
-          const float2 y1 = make_float2(cd[mt][n][2], cd[mt][n][3]);
-          eh2 = __ffma2_rn(y0, y0, eh2);
-          eh2 = __ffma2_rn(y1, y1, eh2);
-        }
+      for (int s4 = 0; s4 < 4; ++s4) {
+        eh2 = __ffma2_rn(make_float2(cd[s4][0], cd[s4][1]), make_float2(cd[s4][0], cd[s4][1]), eh2);
+        eh3 = __ffma2_rn(make_float2(cd[s4][2], cd[s4][3]), make_float2(cd[s4][2], cd[s4][3]), eh3);
       }
     }
-    const float eh = warp_sum(eh2.x + eh2.y);
-    if (p.gate != GATE_CS) {
-      const float el = warp_sum(el2.x + el2.y);
-      return __fdiv_rn(eh * 0.5f, el + 1e-6f);
+    const float2 e = warp_sum2(make_float2(el2.x + el2.y, (eh2.x + eh2.y) + (eh3.x + eh3.y)));
+    float el = need_low ? e.x : 0.f, eh = e.y;
+    if constexpr (P > 1) {  // add the team's panels, in panel order (the same sum in every warp)
+      float2* xb = xch + (ktiles & 1) * P;
+      if (lane == 0) xb[panel] = make_float2(el, eh);
+      team_sync();
+      el = 0.f;
+      eh = 0.f;
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        const float2 v = xb[q];
+        el += v.x;
+        eh += v.y;
+      }
     }
+    ++ktiles;
+    if (need_low) return __fdiv_rn(eh * 0.5f, el + 1e-6f);
     float kn = sqrtf(eh * 0.5f);
     if (kn < 1e-38f) kn = 0.f;
     return qmax * kn;
   };
 
+
   // ======================================================== phase A: K stream
-#ifdef OC_PROBE_SPAN
-  uint64_t span_t0;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(span_t0));
-#endif
-  const int64_t fa = range_lo(wg, N, W), fb = range_lo(wg + 1, N, W);
-  const int nA = (int)(fb - fa);
-  int kept_local = 0, kept_stat = 0;
-  {
-    int u_iss = (nA > 0) ? upper_index(tp, U, fa) : 0;
-    int u_cur = u_iss;
-    int64_t f_iss = fa;
-    auto issue_next = [&]() {
-      while (f_iss >= tp[u_iss + 1]) ++u_iss;
-      issue((uint32_t)(f_iss - fa) % NSLOT, u_iss, tile_of(u_iss, f_iss), false, nullptr, 0);
-      ++f_iss;
+  // ======================================================== single pass
+  // Warp wg owns the flattened K tiles [fa, fb) (unit-major, split-major inside
+  // a unit, so a range interleaves over the sequence).  It gates each tile and
+  // streams the V of a retained tile into the ring slot its K tile just left;
+  // the ring is one FIFO of copies (one cp.async group per slot).  A unit's
+  // state is written once all its K tiles in the range are gated and no V copy
+  // of it is pending: directly when the range holds the whole unit, else as a
+  // partial state merged by the last of the unit's warps.
+  const int64_t WE = (N < W) ? (N > 0 ? N : 1) : W;  // warps with a tile range
+  const bool active = wg < WE;
+  const int64_t fa = active ? range_lo(wg, N, WE) : 0, fb = active ? range_lo(wg + 1, N, WE) : 0;
+  int kept_stat = 0;
+  if constexpr (ATTN) {
+    // units without a tile: zero output (or an empty partial state)
+    if (active)
+      for (int u = (int)wg; u < U; u += (int)WE) {
+        if (tp[u + 1] != tp[u]) continue;
+        const int seq = unit_seq(u), kvh = unit_kvh(u), chunk = unit_chunk(u);
+        for (int g = 0; g < GC && chunk * GC + g < p.group; ++g)
+          for (int d = panel * HDL + lane; d < (panel + 1) * HDL; d += 32)
+            emit(p, seq, kvh * p.group + chunk * GC + g, d, -1e9f, 0.f, 0.f);
+      }
+  }
+    float m_run[GC], l_part[GC];
+    float2 acc[TC ? 1 : GC][D2];
+    // tensor-core path: this lane's query g8 (m, partial l) and O^T fragments
+    float m_mine = -1e9f, l_mine = 0.f;
+    float tacc[TC ? HDL / 16 : 1][4];  // this warp's HDL output columns
+    auto reset_state = [&]() {
+      if constexpr (TC) {
+        m_mine = -1e9f;
+        l_mine = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < HDL / 16; ++mt)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tacc[mt][j] = 0.f;
+        return;
+      }
+#pragma unroll
+      for (int g = 0; g < GC; ++g) {
+        m_run[g] = -1e9f;
+        l_part[g] = 0.f;
+#pragma unroll
+        for (int d = 0; d < D2; ++d) acc[g][d] = make_float2(0.f, 0.f);
+      }
     };
-    for (int i = 0; i < NSLOT; ++i) {
-      if (i < nA) issue_next(); else cp_async_commit();
+    float* part = p.part;
+    constexpr int PST = HDL + 4;  // floats per (slot, g, panel) partial record: acc[HDL], m, l
+    auto rec_of = [&](int64_t sl, int g) { return part + ((sl * GC + g) * P + panel) * PST; };
+
+    // finalize(u, empty): write this warp's state for unit u (empty = no tile of
+    // u retained in this warp's range: an empty state, the accumulator untouched)
+    auto finalize = [&](int u, bool empty) {
+      const int seq = unit_seq(u), kvh = unit_kvh(u), chunk = unit_chunk(u);
+      const int gvalid = (p.group - chunk * GC) < GC ? (p.group - chunk * GC) : GC;
+      const int hq0 = kvh * p.group + chunk * GC;
+      const int64_t R0 = tp[u], R1 = (int64_t)tp[u + 1] - 1;
+      const int64_t w0 = range_owner(R0, N, WE), w1 = range_owner(R1, N, WE);
+      const bool direct = (w0 == w1);
+      const int64_t slot = direct ? 0 : partial_slot(wg, R0, N, WE);
+      // put(query, dim, m, l, acc): write the merged state of one output element
+      auto put = [&](int qq, int d, float m, float l, float a) {
+        if (empty) {
+          m = -1e9f;
+          l = 0.f;
+          a = 0.f;
+        }
+        if (direct) {
+          if (qq < gvalid) emit(p, seq, hq0 + qq, panel * HDL + d, m, l, a);
+        } else if (qq < GC) {
+          rec_of(slot, qq)[d] = a;
+        }
+      };
+      if constexpr (TC) {
+        if (GC <= 4 && !empty) {  // packed P: add the tail columns 4..7 into the head columns 0..3
+#pragma unroll
+          for (int mt = 0; mt < HDL / 16; ++mt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tacc[mt][j] += __shfl_xor_sync(0xffffffffu, tacc[mt][j], 2);
+        }
+        float lq = l_mine + __shfl_xor_sync(0xffffffffu, l_mine, 1);
+        lq += __shfl_xor_sync(0xffffffffu, lq, 2);
+        const int qa = 2 * t4, qb = 2 * t4 + 1;
+        const float ma = __shfl_sync(0xffffffffu, m_mine, (8 * t4) & 31);
+        const float mb = __shfl_sync(0xffffffffu, m_mine, (8 * t4 + 4) & 31);
+        const float la = __shfl_sync(0xffffffffu, lq, (8 * t4) & 31);
+        const float lb = __shfl_sync(0xffffffffu, lq, (8 * t4 + 4) & 31);
+#pragma unroll
+        for (int mt = 0; mt < HDL / 16; ++mt) {
+          put(qa, 16 * mt + g8, ma, la, tacc[mt][0]);
+          put(qb, 16 * mt + g8, mb, lb, tacc[mt][1]);
+          put(qa, 16 * mt + g8 + 8, ma, la, tacc[mt][2]);
+          put(qb, 16 * mt + g8 + 8, mb, lb, tacc[mt][3]);
+        }
+        if (!direct && t4 == 0 && g8 < GC)
+          *reinterpret_cast<float2*>(rec_of(slot, g8) + HDL) =
+              empty ? make_float2(-1e9f, 0.f) : make_float2(m_mine, lq);
+      } else {
+        // sum the row groups' accumulators and the lanes' probability sums
+#pragma unroll
+        for (int o = C; o < 32; o <<= 1)
+          if (!empty)
+#pragma unroll
+          for (int g = 0; g < GC; ++g)
+#pragma unroll
+            for (int d = 0; d < D2; ++d) {
+              acc[g][d].x += __shfl_xor_sync(0xffffffffu, acc[g][d].x, o);
+              acc[g][d].y += __shfl_xor_sync(0xffffffffu, acc[g][d].y, o);
+            }
+        float lsum[GC];
+#pragma unroll
+        for (int g = 0; g < GC; ++g) lsum[g] = warp_sum(l_part[g]);
+        if (rg == 0)
+#pragma unroll
+          for (int g = 0; g < GC; ++g) {
+#pragma unroll
+            for (int d = 0; d < D2; ++d) {
+              put(g, c * DPT + 2 * d, m_run[g], lsum[g], acc[g][d].x);
+              put(g, c * DPT + 2 * d + 1, m_run[g], lsum[g], acc[g][d].y);
+            }
+            if (!direct && c == 0)
+              *reinterpret_cast<float2*>(rec_of(slot, g) + HDL) =
+                  empty ? make_float2(-1e9f, 0.f) : make_float2(m_run[g], lsum[g]);
+          }
+      }
+      if (direct) return;
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      uint32_t* ticket = p.tickets + (int64_t)u * P + panel;  // one merge per (unit, panel)
+      if (lane == 0) last = (atomicAdd(ticket, 1u) == (uint32_t)(w1 - w0)) ? 1 : 0;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) return;
+      __threadfence();
+      if (lane == 0) *ticket = 0u;
+      constexpr int NE = (HDL + 31) / 32;  // columns per lane in the merge
+      for (int g = 0; g < gvalid; ++g) {
+        float M = -INFINITY;
+        for (int64_t w = w0 + lane; w <= w1; w += 32) {
+          const int64_t sl = (w == w0) ? partial_slot(w0, R0, N, WE) : 2 * w;
+          M = fmaxf(M, __ldcg(rec_of(sl, g) + HDL));
+        }
+        M = warp_max(M);
+        float lt = 0.f;
+        float a[NE];
+#pragma unroll
+        for (int e = 0; e < NE; ++e) a[e] = 0.f;
+#pragma unroll 4
+        for (int64_t w = w0; w <= w1; ++w) {
+          const int64_t sl = (w == w0) ? partial_slot(w0, R0, N, WE) : 2 * w;
+          const float* rec = rec_of(sl, g);
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + HDL));
+          const float wt = exp2f(ml.x - M);
+          lt = fmaf(ml.y, wt, lt);
+#pragma unroll
+          for (int e = 0; e < NE; ++e)
+            if (lane + 32 * e < HDL) a[e] = fmaf(__ldcg(rec + lane + 32 * e), wt, a[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < NE; ++e)
+          if (lane + 32 * e < HDL)
+            emit(p, seq, kvh * p.group + chunk * GC + g, panel * HDL + lane + 32 * e, M, lt, a[e]);
+      }
+    };
+
+
+  reset_state();
+
+  float2 qv[TC ? 1 : GC][D2];
+  uint32_t qf[TC ? HDL / 16 : 1][2];  // q (this warp's panel) as mma B fragments (dims x queries), raw 16-bit
+  int q_unit = -1;
+
+  // descriptor of ring slot `lane` (lanes < NSLOT): flattened tile (-1: empty),
+  // V copy flag, unit and tile index
+  int64_t dsc_f = -1;
+  int dsc_v = 0, dsc_u = 0, dsc_t = 0;
+  const int u_first = (fb > fa) ? upper_index(tp, U, fa) : 0;
+  int u_iss = u_first, seq_iss = 0, kvh_iss = 0;
+  int64_t f_iss = fa;
+  SplitIter it_iss;
+  auto enter_unit = [&](int u, int64_t f) {  // issue cursor enters unit u at flattened tile f
+    u_iss = u;
+    seq_iss = unit_seq(u);
+    kvh_iss = unit_kvh(u);
+    it_iss.init((int)(f - tp[u]), tp[u + 1] - tp[u], S);
+  };
+  if (fb > fa) enter_unit(u_first, fa);
+  auto issue_next = [&](uint32_t s) {
+#ifdef OC_PROBE_WAIT
+    const long long i0 = clock64();
+#endif
+    if (f_iss < fb) {
+      if (f_iss >= tp[u_iss + 1]) {
+        int u = u_iss + 1;
+        while (f_iss >= tp[u + 1]) ++u;
+        enter_unit(u, f_iss);
+      }
+      const int tile = it_iss.tile();
+      issue(s, seq_iss, kvh_iss, tile, false);
+      if (lane == (int)s) {
+        dsc_f = f_iss;
+        dsc_v = 0;
+        dsc_u = u_iss;
+        dsc_t = tile;
+      }
+      it_iss.next();
+      ++f_iss;
+    } else if (lane == (int)s) {
+      dsc_f = -1;
     }
+#ifdef OC_PROBE_WAIT
+    pw_iss += clock64() - i0;
+#endif
+  };
+  for (uint32_t s = 0; s < NSLOT; ++s) issue_next(s);
 
-    float2 qv[TC ? 1 : GC][D2];
-    uint32_t qf[TC ? HD / 16 : 1][2];  // q as mma B fragments (dims x queries), raw 16-bit
-    int q_unit = -1;
-    int seg_unit = -1, seg_kept = 0;
+  int u_k = -1, kept_k = 0;  // unit of the last gated K tile and its retained tiles in the range
+  int seq_k = 0, kvh_k = 0, chunk_k = 0;
+  int64_t f_gated = fa;              // K tiles [fa, f_gated) are gated
+  int acc_unit = -1;                 // unit held by the accumulator
 
-    for (int i = 0; i < nA; ++i) {
-      const int64_t f = fa + i;
-      while (f >= tp[u_cur + 1]) ++u_cur;
-      const int u = u_cur;
-      const int tile = tile_of(u, f);
-      if (u != seg_unit) {
-        if (ATTN && seg_unit >= 0 && seg_kept && lane == 0) atomicAdd(p.cnt_unit + seg_unit, (uint32_t)seg_kept);
-        seg_unit = u;
-        seg_kept = 0;
+  for (uint32_t j = 0;; ++j) {
+    const uint32_t s = j % NSLOT;
+    if (!__any_sync(0xffffffffu, lane < NSLOT && dsc_f >= 0)) break;
+    const int64_t f = __shfl_sync(0xffffffffu, dsc_f, s);
+    const int isv = __shfl_sync(0xffffffffu, dsc_v, s);
+    const int u = __shfl_sync(0xffffffffu, dsc_u, s);
+    const int tile = __shfl_sync(0xffffffffu, dsc_t, s);
+    if (f < 0) {
+      issue_next(s);
+      continue;
+    }
+    unsigned char* ts = wait_slot(s);
+    float* lgs = lgs_base + s * (CF::LGB / 4);
+    if (!isv) {
+      // ================================================ K tile: gate (+ logits)
+      if (u != u_k) {
+        u_k = u;
+        kept_k = 0;
+        seq_k = unit_seq(u);
+        kvh_k = unit_kvh(u);
+        chunk_k = unit_chunk(u);
       }
       if constexpr (ATTN) {
         if (u != q_unit) {
           q_unit = u;
-          const int seq = unit_seq(u), kvh = unit_kvh(u), chunk = unit_chunk(u);
+          const int seq = seq_k, kvh = kvh_k, chunk = chunk_k;
           const int64_t qb = (int64_t)seq * p.q_seq_stride;
           if constexpr (TC) {
             const int hq = chunk * GC + g8;
             const bool ok = g8 < GC && hq < p.group;
-            const uint16_t* qrow = static_cast<const uint16_t*>(p.q) + qb + (int64_t)(kvh * p.group + hq) * p.q_head_stride;
+            const uint16_t* qrow = static_cast<const uint16_t*>(p.q) + qb +
+                                   (int64_t)(kvh * p.group + hq) * p.q_head_stride + panel * HDL;
 #pragma unroll
-            for (int ks = 0; ks < HD / 16; ++ks) {
+            for (int ks = 0; ks < HDL / 16; ++ks) {
               qf[ks][0] = ok ? (uint32_t)qrow[16 * ks + 2 * t4] | ((uint32_t)qrow[16 * ks + 2 * t4 + 1] << 16) : 0u;
               qf[ks][1] = ok ? (uint32_t)qrow[16 * ks + 2 * t4 + 8] | ((uint32_t)qrow[16 * ks + 2 * t4 + 9] << 16) : 0u;
             }
@@ -635,18 +854,16 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
         }
       }
 
-#ifdef OC_PROBE_TIMING
-      const uint32_t t_w0 = (uint32_t)clock();
-#endif
-      const unsigned char* ts = wait_item(item);
-#ifdef OC_PROBE_TIMING
-      const uint32_t t_w1 = (uint32_t)clock();
-#endif
-
       // ---- band energies
       float score;
       if constexpr (TC) {
+#ifdef OC_PROBE_WAIT
+        const long long g0 = clock64();
         score = tc_gate(ts);
+        pw_gate += clock64() - g0;
+#else
+        score = tc_gate(ts);
+#endif
       } else {
         float2 sres[NRES][D2];
         float2 ehd[D2];  // one E_high accumulator per column pair: independent FMA chains
@@ -657,7 +874,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
 #pragma unroll
           for (int d = 0; d < D2; ++d) sres[k][d] = make_float2(0.f, 0.f);
 #pragma unroll kUnrollPairs
-        for (int i0 = 0; i0 < (kGateMath ? PAIRS : 0); i0 += NRES) {
+        for (int i0 = 0; i0 < PAIRS; i0 += NRES) {
 #pragma unroll
           for (int k = 0; k < NRES; ++k) {
             const int i2 = i0 + k;
@@ -735,32 +952,32 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
       else if (p.gate == GATE_ZETA_MASK) keep = (score <= p.thr);
       else keep = !(score <= p.thr);
 
-#if !defined(OC_PROBE_TIMING) && !defined(OC_PROBE_SPAN)
-      if (lane == 0 && unit_chunk(u) == 0) {
-        const int64_t mi = (int64_t)(unit_seq(u) * p.num_kv_heads + unit_kvh(u)) * p.num_tiles + tile;
+      if (lane == 0 && panel == 0 && chunk_k == 0) {
+        const int64_t mi = (int64_t)(seq_k * p.num_kv_heads + kvh_k) * p.num_tiles + tile;
         if (p.mask) p.mask[mi] = keep ? 1 : 0;
         if (p.score) p.score[mi] = score;
       }
-#endif
+      f_gated = f + 1;
+      bool v_issued = false;
       if (keep) {
-        if (unit_chunk(u) == 0) ++kept_stat;
+        if (chunk_k == 0 && panel == 0) ++kept_stat;
         if constexpr (ATTN) {
-          const int64_t pos = fa + kept_local;
+          ++kept_k;
           if constexpr (TC) {
-            // logits = K (tokens x dims) * q (dims x queries): 4 token tiles of 16
+            // logits = K (tokens x dims) * q (dims x queries): 4 token tiles of
+            // 16, over this warp's panel (the team adds the panels' partials)
             const uint32_t base = smem_u32(ts);
             float cq[4][4] = {};
 #pragma unroll
-            for (int ks = 0; ks < HD / 16; ++ks)
+            for (int ks = 0; ks < HDL / 16; ++ks)
 #pragma unroll
               for (int mt = 0; mt < 4; ++mt) {
                 uint32_t a4[4];
-                ldsm_x4(tc_addr(base, 16 * mt + (lane & 7) + ((lane >> 3) & 1) * 8, 16 * ks + ((lane >> 4) & 1) * 8,
-                                CF::ROWK), a4);
+                ldsm_x4(base + offL + mt * 2048 + ch4[ks], a4);  // tc_addr(16 mt + x + 8 b3, 16 ks + 8 b4)
                 mma16816<KBF16>(cq[mt], a4, qf[ks][0], qf[ks][1]);
               }
             // C(token, query): lane holds tokens 16mt+g8 (+8), queries 2t4, 2t4+1
-            float* dstl = p.lg + pos * (GC * 64);
+            float* dstl = lgs;
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
@@ -786,7 +1003,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
             }
             reduce_scatter<NV, C>(lg, c);
             // lane c holds indices [c*2GC, (c+1)*2GC): g = idx / RPL, m = idx % RPL
-            float* dstl = p.lg + pos * (GC * 64);
+            float* dstl = lgs;
 #pragma unroll
             for (int h = 0; h < 2 * GC; h += 2) {
               const int idx = c * 2 * GC + h;
@@ -794,269 +1011,53 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
               *reinterpret_cast<float2*>(dstl + g * 64 + rg * RPL + m) = make_float2(lg[h], lg[h + 1]);
             }
           }
-          if (lane == 0) p.list[pos] = (int32_t)f;
-          ++kept_local;
-          ++seg_kept;
+          __syncwarp();  // K tile read, logits stored: the slot takes this tile's V
+          issue(s, seq_k, kvh_k, tile, true);
+          if (lane == (int)s) dsc_v = 1;
+          v_issued = true;
         }
       }
-      __syncwarp();
-      ++item;
-#ifdef OC_PROBE_TIMING
-      const uint32_t t_i0 = (uint32_t)clock();
-#endif
-      if (f_iss < fb) issue_next(); else cp_async_commit();
-#ifdef OC_PROBE_TIMING
-      if (lane == 0 && blockIdx.x == 0 && p.score && i < 16) {
-        uint32_t* pr = reinterpret_cast<uint32_t*>(p.score) + (warp * 16 + i) * 4;
-        pr[0] = t_w0;
-        pr[1] = t_w1;
-        pr[2] = t_i0;
-        pr[3] = (uint32_t)clock();
+      if (!v_issued) {
+        __syncwarp();
+        issue_next(s);
       }
-#endif
-    }
-    if (ATTN && seg_unit >= 0 && seg_kept && lane == 0) atomicAdd(p.cnt_unit + seg_unit, (uint32_t)seg_kept);
-  }
-  if (p.stats && lane == 0 && kept_stat) atomicAdd(p.stats, (uint32_t)kept_stat);
-#ifdef OC_PROBE_SPAN
-  if (lane == 0 && p.score) {
-    uint64_t span_t1;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(span_t1));
-    reinterpret_cast<uint64_t*>(p.score)[2 * wg] = span_t0;
-    reinterpret_cast<uint64_t*>(p.score)[2 * wg + 1] = span_t1;
-  }
-#endif
-  if constexpr (!ATTN) return;
-
-  if constexpr (ATTN) {
-    if (lane == 0) p.cnt_warp[wg] = (uint32_t)kept_local;
-    // ======================================================== grid barrier
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      atomicAdd(p.gbar, 1u);
-      uint32_t n = 0;
-      while (ld_acquire_gpu(p.gbar) < gridDim.x) {
-        if (++n > kWaitLimit) {
-          atomicOr(p.status, ST_TIMEOUT);
-          break;
-        }
-        __nanosleep(64);
+      if constexpr (ATTN) {
+        const int64_t uend = tp[u + 1] < fb ? tp[u + 1] : fb;
+        if (f + 1 == uend && kept_k == 0) finalize(u, true);
       }
-    }
-    __syncthreads();
-    for (int u = tid; u < U; u += blockDim.x) kp[u + 1] = (int)__ldcg(p.cnt_unit + u);
-    for (int w = tid; w < W; w += blockDim.x) pa[w + 1] = (int)__ldcg(p.cnt_warp + w);
-    block_scan(kp, U, scan_tmp);
-    block_scan(pa, (int)W, scan_tmp);
-    if (tid == 0) misc[0] = (atomicAdd(p.gbar + 1, 1u) == gridDim.x - 1) ? 1 : 0;
-    __syncthreads();
-    if (misc[0]) {  // every CTA has read the counters: reset them for the next launch
-      for (int u = tid; u < U; u += blockDim.x) p.cnt_unit[u] = 0u;
-      if (tid == 0) {
-        p.gbar[0] = 0u;
-        p.gbar[1] = 0u;
-      }
-    }
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-
-    // ======================================================== phase B: V stream
-    const int64_t Kt = pa[W];
-    const int64_t WB = Kt < W ? Kt : W;
-    // units without a retained tile: zero output (or an empty partial state)
-    for (int u = (int)wg; u < U; u += (int)W) {
-      if (kp[u + 1] != kp[u]) continue;
-      const int seq = unit_seq(u), kvh = unit_kvh(u), chunk = unit_chunk(u);
-      for (int g = 0; g < GC && chunk * GC + g < p.group; ++g)
-        for (int d = lane; d < HD; d += 32) emit(p, seq, kvh * p.group + chunk * GC + g, d, -1e9f, 0.f, 0.f);
-    }
-    if (wg >= WB) return;
-    const int64_t ra = range_lo(wg, Kt, WB), rb = range_lo(wg + 1, Kt, WB);
-    const int nB = (int)(rb - ra);
-
-    // retained tile of rank r -> (list position, flattened index)
-    auto fetch = [&](int64_t r, int64_t& pos, int64_t& f) {
-      const int wa = upper_index(pa, (int)W, r);
-      pos = range_lo(wa, N, W) + (r - pa[wa]);
-      f = __ldcg(p.list + pos);
-    };
-    // lanes hold two windows of 32 ranks: [chunk_base, +32) and the next one
-    int64_t cpos = 0, cf = 0, npos = 0, nf = 0;
-    if (lane < nB) fetch(ra + lane, cpos, cf);
-    if (32 + lane < nB) fetch(ra + 32 + lane, npos, nf);
-    int chunk_base = 0;
-    auto item_at = [&](int j, int64_t& pos, int64_t& f) {  // j in [chunk_base, chunk_base + 64)
-      const bool cur = j < chunk_base + 32;
-      const int src = (j - chunk_base) & 31;
-      pos = __shfl_sync(0xffffffffu, cur ? cpos : npos, src);
-      f = __shfl_sync(0xffffffffu, cur ? cf : nf, src);
-    };
-
-    int u_iss = 0, u_cur = 0;
-    if (nB > 0) {
-      int64_t pos0, f0;
-      item_at(0, pos0, f0);
-      u_iss = u_cur = upper_index(tp, U, f0);
-    }
-    int j_iss = 0;
-    const uint32_t item0 = item;
-    auto issue_next_v = [&]() {
-      int64_t pos, f;
-      item_at(j_iss, pos, f);
-      while (f >= tp[u_iss + 1]) ++u_iss;
-      issue((item0 + j_iss) % NSLOT, u_iss, tile_of(u_iss, f), true, p.lg + pos * (GC * 64), GC * 64 * 4);
-      ++j_iss;
-    };
-    for (int i = 0; i < NSLOT; ++i) {
-      if (i < nB) issue_next_v(); else cp_async_commit();
-    }
-
-    float m_run[GC], l_part[GC];
-    float2 acc[TC ? 1 : GC][D2];
-    // tensor-core path: this lane's query g8 (m, partial l) and O^T fragments
-    float m_mine = -1e9f, l_mine = 0.f;
-    float tacc[TC ? HD / 16 : 1][4];
-    int cur_unit = -1;
-    auto reset_state = [&]() {
+    } else {
+      // ================================================ V tile of a retained tile
+      acc_unit = u;
       if constexpr (TC) {
-        m_mine = -1e9f;
-        l_mine = 0.f;
+        // B = P (tokens x 8 columns).  Up to 4 queries: column n carries the
+        // 16-bit head (n < 4) or tail (n >= 4) of query n & 3, so one MMA adds
+        // both halves; with more queries head and tail take one MMA each.
+        // This lane computes P for query qg = column g8 (mod 4 when packed).
+        constexpr bool PACK = GC <= 4;
+        const int qg = PACK ? (g8 & 3) : g8;
+        const bool qok = qg < GC;
+        // logits: the sum of the team's panel partials, in panel order
+        team_sync();
+        auto lg2 = [&](int o) -> float2 {
+          if constexpr (P == 1) {
+            return *reinterpret_cast<const float2*>(lgs + o);
+          } else {
+            float2 t = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int mt = 0; mt < HD / 16; ++mt)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) tacc[mt][j] = 0.f;
-        return;
-      }
-#pragma unroll
-      for (int g = 0; g < GC; ++g) {
-        m_run[g] = -1e9f;
-        l_part[g] = 0.f;
-#pragma unroll
-        for (int d = 0; d < D2; ++d) acc[g][d] = make_float2(0.f, 0.f);
-      }
-    };
-    float* part = p.part;
-    constexpr int PST = HD + 4;  // floats per (slot, g) partial record
-
-    auto finalize = [&](int u) {
-      const int seq = unit_seq(u), kvh = unit_kvh(u), chunk = unit_chunk(u);
-      const int gvalid = (p.group - chunk * GC) < GC ? (p.group - chunk * GC) : GC;
-      const int hq0 = kvh * p.group + chunk * GC;
-      const int64_t R0 = kp[u], R1 = (int64_t)kp[u + 1] - 1;
-      const int64_t w0 = range_owner(R0, Kt, WB), w1 = range_owner(R1, Kt, WB);
-      const bool direct = (w0 == w1);
-      const int64_t slot = direct ? 0 : partial_slot(wg, R0, Kt, WB);
-      // put(query, dim, m, l, acc): write the merged state of one output element
-      auto put = [&](int qq, int d, float m, float l, float a) {
-        if (direct) {
-          if (qq < gvalid) emit(p, seq, hq0 + qq, d, m, l, a);
-        } else if (qq < GC) {
-          part[(slot * GC + qq) * PST + d] = a;
-        }
-      };
-      if constexpr (TC) {
-        float lq = l_mine + __shfl_xor_sync(0xffffffffu, l_mine, 1);
-        lq += __shfl_xor_sync(0xffffffffu, lq, 2);
-        const int qa = 2 * t4, qb = 2 * t4 + 1;
-        const float ma = __shfl_sync(0xffffffffu, m_mine, (8 * t4) & 31);
-        const float mb = __shfl_sync(0xffffffffu, m_mine, (8 * t4 + 4) & 31);
-        const float la = __shfl_sync(0xffffffffu, lq, (8 * t4) & 31);
-        const float lb = __shfl_sync(0xffffffffu, lq, (8 * t4 + 4) & 31);
-#pragma unroll
-        for (int mt = 0; mt < HD / 16; ++mt) {
-          put(qa, 16 * mt + g8, ma, la, tacc[mt][0]);
-          put(qb, 16 * mt + g8, mb, lb, tacc[mt][1]);
-          put(qa, 16 * mt + g8 + 8, ma, la, tacc[mt][2]);
-          put(qb, 16 * mt + g8 + 8, mb, lb, tacc[mt][3]);
-        }
-        if (!direct && t4 == 0 && g8 < GC)
-          *reinterpret_cast<float2*>(part + (slot * GC + g8) * PST + HD) = make_float2(m_mine, lq);
-      } else {
-        // sum the row groups' accumulators and the lanes' probability sums
-#pragma unroll
-        for (int o = C; o < 32; o <<= 1)
-#pragma unroll
-          for (int g = 0; g < GC; ++g)
-#pragma unroll
-            for (int d = 0; d < D2; ++d) {
-              acc[g][d].x += __shfl_xor_sync(0xffffffffu, acc[g][d].x, o);
-              acc[g][d].y += __shfl_xor_sync(0xffffffffu, acc[g][d].y, o);
+            for (int q = 0; q < P; ++q) {
+              const float2 v = *reinterpret_cast<const float2*>(lgs_all + ((team * P + q) * NSLOT + s) * (CF::LGB / 4) + o);
+              t.x += v.x;
+              t.y += v.y;
             }
-        float lsum[GC];
-#pragma unroll
-        for (int g = 0; g < GC; ++g) lsum[g] = warp_sum(l_part[g]);
-        if (rg == 0)
-#pragma unroll
-          for (int g = 0; g < GC; ++g) {
-#pragma unroll
-            for (int d = 0; d < D2; ++d) {
-              put(g, c * DPT + 2 * d, m_run[g], lsum[g], acc[g][d].x);
-              put(g, c * DPT + 2 * d + 1, m_run[g], lsum[g], acc[g][d].y);
-            }
-            if (!direct && c == 0)
-              *reinterpret_cast<float2*>(part + (slot * GC + g) * PST + HD) = make_float2(m_run[g], lsum[g]);
+            return t;
           }
-      }
-      if (direct) return;
-      __threadfence();
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) last = (atomicAdd(p.tickets + u, 1u) == (uint32_t)(w1 - w0)) ? 1 : 0;
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) return;
-      __threadfence();
-      if (lane == 0) p.tickets[u] = 0u;
-      constexpr int NE = (HD + 31) / 32;  // head_dim columns per lane in the merge
-      for (int g = 0; g < gvalid; ++g) {
-        float M = -INFINITY;
-        for (int64_t w = w0 + lane; w <= w1; w += 32) {
-          const int64_t sl = (w == w0) ? partial_slot(w0, R0, Kt, WB) : 2 * w;
-          M = fmaxf(M, __ldcg(part + (sl * GC + g) * PST + HD));
-        }
-        M = warp_max(M);
-        float lt = 0.f;
-        float a[NE];
-#pragma unroll
-        for (int e = 0; e < NE; ++e) a[e] = 0.f;
-#pragma unroll 4
-        for (int64_t w = w0; w <= w1; ++w) {
-          const int64_t sl = (w == w0) ? partial_slot(w0, R0, Kt, WB) : 2 * w;
-          const float* rec = part + (sl * GC + g) * PST;
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + HD));
-          const float wt = exp2f(ml.x - M);
-          lt = fmaf(ml.y, wt, lt);
-#pragma unroll
-          for (int e = 0; e < NE; ++e)
-            if (lane + 32 * e < HD) a[e] = fmaf(__ldcg(rec + lane + 32 * e), wt, a[e]);
-        }
-#pragma unroll
-        for (int e = 0; e < NE; ++e)
-          if (lane + 32 * e < HD) emit(p, seq, kvh * p.group + chunk * GC + g, lane + 32 * e, M, lt, a[e]);
-      }
-    };
-
-    reset_state();
-    for (int i = 0; i < nB; ++i) {
-      int64_t pos, f;
-      item_at(i, pos, f);
-      while (f >= tp[u_cur + 1]) ++u_cur;
-      if (u_cur != cur_unit) {
-        if (cur_unit >= 0) finalize(cur_unit);
-        reset_state();
-        cur_unit = u_cur;
-      }
-      unsigned char* ts = const_cast<unsigned char*>(wait_item(item));
-      float* lgs = reinterpret_cast<float*>(ts + 64 * CF::ROWMAX);
-      if constexpr (TC) {
-        // this lane's query g8: logits of tokens 16ks + 2t4 + {0,1,8,9}
+        };
         float lv[4][4];
         float lmax = -INFINITY;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-          const float2 x = g8 < GC ? *reinterpret_cast<const float2*>(lgs + g8 * 64 + 16 * ks + 2 * t4)
-                                   : make_float2(-INFINITY, -INFINITY);
-          const float2 y = g8 < GC ? *reinterpret_cast<const float2*>(lgs + g8 * 64 + 16 * ks + 2 * t4 + 8)
-                                   : make_float2(-INFINITY, -INFINITY);
+          const float2 x = qok ? lg2(qg * 64 + 16 * ks + 2 * t4) : make_float2(-INFINITY, -INFINITY);
+          const float2 y = qok ? lg2(qg * 64 + 16 * ks + 2 * t4 + 8) : make_float2(-INFINITY, -INFINITY);
           lv[ks][0] = x.x; lv[ks][1] = x.y; lv[ks][2] = y.x; lv[ks][3] = y.y;
           lmax = fmaxf(lmax, fmaxf(fmaxf(x.x, x.y), fmaxf(y.x, y.y)));
         }
@@ -1073,7 +1074,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
           float pr[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            pr[j] = g8 < GC ? exp2f(lv[ks][j] - nm) : 0.f;
+            pr[j] = qok ? exp2f(lv[ks][j] - nm) : 0.f;
             psum += pr[j];
           }
 #pragma unroll
@@ -1092,26 +1093,31 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
               bl[ks][h] = *reinterpret_cast<const uint32_t*>(&lo);
             }
           }
+          if constexpr (PACK) {
+            if (g8 >= 4) {
+              bh[ks][0] = bl[ks][0];
+              bh[ks][1] = bl[ks][1];
+            }
+          }
         }
         l_mine = fmaf(l_mine, alpha, psum);
-        // rescale the O^T columns (queries 2t4, 2t4+1) by their alphas
+        // rescale the O^T columns 2t4, 2t4+1 by the alphas of their queries
         const float a0 = __shfl_sync(0xffffffffu, alpha, (8 * t4) & 31);
         const float a1 = __shfl_sync(0xffffffffu, alpha, (8 * t4 + 4) & 31);
 #pragma unroll
-        for (int mt = 0; mt < HD / 16; ++mt) {
+        for (int mt = 0; mt < HDL / 16; ++mt) {
           tacc[mt][0] *= a0; tacc[mt][1] *= a1; tacc[mt][2] *= a0; tacc[mt][3] *= a1;
         }
-        // O^T (dims x queries) += V^T (dims x tokens) * P (tokens x queries)
+        // O^T (dims x columns) += V^T (dims x tokens) * P (tokens x columns)
         const uint32_t base = smem_u32(ts);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
-          for (int mt = 0; mt < HD / 16; ++mt) {
+          for (int mt = 0; mt < HDL / 16; ++mt) {
             uint32_t a4[4];
-            ldsm_x4_t(tc_addr(base, 16 * ks + (lane & 7) + ((lane >> 4) & 1) * 8, 16 * mt + ((lane >> 3) & 1) * 8,
-                              CF::ROWV), a4);
+            ldsm_x4_t(base + offV + ks * 2048 + ch3[mt], a4);  // tc_addr(16 ks + x + 8 b4, 16 mt + 8 b3)
             mma16816<KBF16>(tacc[mt], a4, bh[ks][0], bh[ks][1]);
-            mma16816<KBF16>(tacc[mt], a4, bl[ks][0], bl[ks][1]);
+            if constexpr (!PACK) mma16816<KBF16>(tacc[mt], a4, bl[ks][0], bl[ks][1]);
           }
       } else {
         // per query head: tile max, rescale, probabilities written back in place
@@ -1148,23 +1154,32 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT>::NT, 1)
         }
       }
       __syncwarp();
-      ++item;
-      if (j_iss < nB) issue_next_v(); else cp_async_commit();
-      // slide the rank window once the process cursor leaves the current 32
-      if (i + 1 == chunk_base + 32) {
-        cpos = npos;
-        cf = nf;
-        chunk_base += 32;
-        if (chunk_base + 32 + lane < nB) fetch(ra + chunk_base + 32 + lane, npos, nf);
+      issue_next(s);
+    }
+    if constexpr (ATTN) {
+      if (acc_unit >= 0) {
+        const int64_t ua = tp[acc_unit], uend = tp[acc_unit + 1] < fb ? tp[acc_unit + 1] : fb;
+        if (f_gated >= uend &&
+            !__any_sync(0xffffffffu, lane < NSLOT && dsc_f >= ua && dsc_f < uend && dsc_v != 0)) {
+          finalize(acc_unit, false);
+          acc_unit = -1;
+          reset_state();
+        }
       }
     }
-    if (cur_unit >= 0) finalize(cur_unit);
   }
+  if (p.stats && lane == 0 && kept_stat) atomicAdd(p.stats, (uint32_t)kept_stat);
+#ifdef OC_PROBE_WAIT
+  if (lane == 0 && (blockIdx.x % 50 == 0))
+    printf("PW blk %d w %d items %d cyc/item %lld wait %lld gate %lld issue %lld\n", blockIdx.x, warp, pw_n,
+           (clock64() - pw_t0) / (pw_n ? pw_n : 1), pw_wait / (pw_n ? pw_n : 1), pw_gate / (pw_n ? pw_n : 1), pw_iss / (pw_n ? pw_n : 1));
+#endif
 }
 
 template <typename KT, typename VT, int HD, int GC, bool ATTN, int NSLOT, bool TC>
-cudaError_t launch_decode(const DecodeParams& p, int num_sms, cudaStream_t stream) {
-  using CF = Cfg<KT, VT, HD, GC, ATTN, NSLOT>;
+cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int num_sms,
+                          cudaStream_t stream) {
+  using CF = Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>;
   auto kern = decode_kernel<KT, VT, HD, GC, ATTN, NSLOT, TC>;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1181,8 +1196,9 @@ cudaError_t launch_decode(const DecodeParams& p, int num_sms, cudaStream_t strea
   }
   const int nchunks = (p.group + GC - 1) / GC;
   const int64_t tiles = (int64_t)p.num_seqs * p.num_kv_heads * nchunks * p.num_tiles;
-  // about two tiles per warp, at most one wave of resident CTAs
-  const int64_t want = (tiles + 2 * CF::NW - 1) / (2 * CF::NW);
+  // about two tiles per team, at most one wave of resident CTAs
+  constexpr int kTeams = CF::NW / CF::P;
+  const int64_t want = (tiles + 2 * kTeams - 1) / (2 * kTeams);
   const int64_t cap = (int64_t)num_sms * resident[dev];
   int64_t grid = want < 1 ? 1 : (want > cap ? cap : want);
   if (grid * CF::NW > CF::MAXW) grid = CF::MAXW / CF::NW;
@@ -1191,12 +1207,8 @@ cudaError_t launch_decode(const DecodeParams& p, int num_sms, cudaStream_t strea
   cfg.blockDim = dim3(CF::NT);
   cfg.dynamicSmemBytes = CF::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = ATTN ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, p);
+  cfg.numAttrs = 0;
+  return cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
 }
 
 }  // namespace oc

@@ -16,32 +16,34 @@ namespace oc {
 constexpr int kSlots = OC_SLOTS;  // per-warp ring depth
 
 template <typename VT, int HD, bool TC>
-static cudaError_t launch_gc_tc(const DecodeParams& p, int gc, bool attn, int sms, cudaStream_t st) {
-  if (!attn) return launch_decode<OC_KT, OC_KT, HD, 1, false, kSlots, TC>(p, sms, st);
+static cudaError_t launch_gc_tc(const DecodeParams& p, const TensorMaps& m, int gc, bool attn, int sms,
+                                cudaStream_t st) {
+  if (!attn) return launch_decode<OC_KT, OC_KT, HD, 1, false, kSlots, TC>(p, m.k, m.v, sms, st);
   switch (gc) {
-    case 1: return launch_decode<OC_KT, VT, HD, 1, true, kSlots, TC>(p, sms, st);
-    case 2: return launch_decode<OC_KT, VT, HD, 2, true, kSlots, TC>(p, sms, st);
-    case 4: return launch_decode<OC_KT, VT, HD, 4, true, kSlots, TC>(p, sms, st);
-    default: return launch_decode<OC_KT, VT, HD, 8, true, kSlots, TC>(p, sms, st);
+    case 1: return launch_decode<OC_KT, VT, HD, 1, true, kSlots, TC>(p, m.k, m.v, sms, st);
+    case 2: return launch_decode<OC_KT, VT, HD, 2, true, kSlots, TC>(p, m.k, m.v, sms, st);
+    case 4: return launch_decode<OC_KT, VT, HD, 4, true, kSlots, TC>(p, m.k, m.v, sms, st);
+    default: return launch_decode<OC_KT, VT, HD, 8, true, kSlots, TC>(p, m.k, m.v, sms, st);
   }
 }
 
 // tensor-core path: 16-bit keys with values of the same type, head_dim >= 64
 template <typename VT, int HD>
-static cudaError_t launch_gc(const DecodeParams& p, int gc, bool attn, int sms, cudaStream_t st, bool tc) {
+static cudaError_t launch_gc(const DecodeParams& p, const TensorMaps& m, int gc, bool attn, int sms,
+                             cudaStream_t st, bool tc) {
   constexpr bool kTcOk = sizeof(OC_KT) == 2 && std::is_same<VT, OC_KT>::value && HD >= 64;
   if constexpr (kTcOk) {
-    if (tc) return launch_gc_tc<VT, HD, true>(p, gc, attn, sms, st);
+    if (tc) return launch_gc_tc<VT, HD, true>(p, m, gc, attn, sms, st);
   }
-  return launch_gc_tc<VT, HD, false>(p, gc, attn, sms, st);
+  return launch_gc_tc<VT, HD, false>(p, m, gc, attn, sms, st);
 }
 
 // One head_dim per translation unit (OC_HEADDIM): int dispatch_<kname>_<hd>(...)
-int OC_CAT(OC_CAT(OC_CAT(dispatch_, OC_KNAME), _), OC_HEADDIM)(const DecodeParams& p, int v_dtype, int gc, bool attn,
-                                                              int sms, cudaStream_t st, bool tc) {
+int OC_CAT(OC_CAT(OC_CAT(dispatch_, OC_KNAME), _), OC_HEADDIM)(const DecodeParams& p, const TensorMaps& m, int v_dtype,
+                                                              int gc, bool attn, int sms, cudaStream_t st, bool tc) {
 #define OC_CASE(code, VT)                                                 \
   if (v_dtype == code || !attn) {                                         \
-    const cudaError_t e = launch_gc<VT, OC_HEADDIM>(p, gc, attn, sms, st, tc);     \
+    const cudaError_t e = launch_gc<VT, OC_HEADDIM>(p, m, gc, attn, sms, st, tc);     \
     return e == cudaSuccess ? 0 : 4;                                      \
   }
   OC_VTYPES(OC_CASE)

@@ -18,7 +18,7 @@
 
 namespace {
 
-constexpr size_t kScratchBytes = size_t(32) << 20;  // 32 MiB per device
+constexpr size_t kScratchBytes = size_t(2) << 20;  // 2 MiB per device
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;

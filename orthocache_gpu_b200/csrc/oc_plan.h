@@ -18,8 +18,10 @@
 
 #if defined(__CUDACC__)
 #define OC_HD __host__ __device__ __forceinline__
+#define OC_HD_MEMBER __host__ __device__ __forceinline__
 #else
 #define OC_HD static inline
+#define OC_HD_MEMBER inline
 #endif
 
 namespace oc {
@@ -46,6 +48,34 @@ OC_HD int split_major_tile(int k, int T, int S) {
   }
   return s + j * S;
 }
+
+// Iterator over a unit's tiles in split-major order (the sequence
+// split_major_tile(0..T-1, T, S) without a division per step).
+struct SplitIter {
+  int s, j, q, r, S;
+  OC_HD_MEMBER void init(int k, int T, int S_) {
+    if (S_ <= 1 || T <= 0) {
+      S = 1; q = T; r = 0; s = 0; j = k;
+      return;
+    }
+    S = S_; q = T / S_; r = T % S_;
+    if (k < r * (q + 1)) {
+      s = k / (q + 1);
+      j = k % (q + 1);
+    } else {
+      const int k2 = k - r * (q + 1);
+      s = r + k2 / q;
+      j = k2 % q;
+    }
+  }
+  OC_HD_MEMBER int tile() const { return s + j * S; }
+  OC_HD_MEMBER void next() {
+    if (++j >= q + (s < r ? 1 : 0)) {
+      ++s;
+      j = 0;
+    }
+  }
+};
 
 // Partial-state slot of phase-B warp w for a unit whose first retained rank is R0.
 OC_HD int64_t partial_slot(int64_t w, int64_t R0, int64_t Kt, int64_t WB) {

@@ -135,4 +135,22 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
   }
 }
 
+// Tiled TMA load of one box of a 4-D tensor map into this CTA's shared
+// memory, completing (as transaction bytes) on mbarrier `bar`.  Coordinates
+// are element indices, innermost first.  No multicast.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cta.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(pol)
+      : "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (TMA) writes to the same addresses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 }  // namespace oc

@@ -38,7 +38,11 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert l.oc_auto_num_splits(16, 148) == 4
     assert l.oc_auto_num_splits(0, 148) == 1
     assert l.oc_auto_num_splits(10000, 148) == 148
-    assert l.oc_workspace_bytes(32, 1, 512, 128) >= 32 * 512 * (64 * 4 + 4)
+    # tickets + two partial states (acc, m, l) per team of warps; no per-tile scratch
+    ws = l.oc_workspace_bytes(32, 1, 512, 128)
+    assert ws >= 2 * 1280 * (128 + 4) * 4
+    assert ws == l.oc_workspace_bytes(4096, 1, 1 << 20, 128)
+    assert l.oc_workspace_bytes(32, 8, 512, 128) > ws
     assert l.oc_status_string(3).decode().startswith("workspace")
 
 

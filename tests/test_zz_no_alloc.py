@@ -57,15 +57,17 @@ def test_noalloc_entry_point_matches_workspace_entry_point():
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
+    # head_dim 256 needs about 2.8 MiB of split-K scratch, more than the 2 MiB
+    # reserved array: refused before any memory is touched
     lib = _lib.load()
     dev = torch.device("cuda", 0)
-    q = torch.zeros(4096, 128, dtype=torch.float16, device=dev)
-    kv = torch.zeros(4096, 64 * 1024, 128, dtype=torch.float16, device="meta")  # never touched
+    q = torch.zeros(2, 256, dtype=torch.float16, device=dev)
     out = torch.empty_like(q)
     ctrl = torch.zeros(2, dtype=torch.int32, device=dev)
+    seq = 64 * 16
     rc = lib.oc_fused_attention_v2_noalloc(
-        q.data_ptr(), _lib.OC_F16, 128, 16, _lib.OC_F16, kv.stride(0), 128, 16, _lib.OC_F16, kv.stride(0), 128,
-        4096, 64 * 1024, 128, 1.0, 512, 148, out.data_ptr(), _lib.OC_F16, 128, None, None,
+        q.data_ptr(), _lib.OC_F16, 256, 16, _lib.OC_F16, seq * 256, 256, 16, _lib.OC_F16, seq * 256, 256,
+        2, seq, 256, 1.0, 0, 148, out.data_ptr(), _lib.OC_F16, 256, None, None,
         ctrl[1:].data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == 5
-    assert "32 MiB" in lib.oc_status_string(rc).decode()
+    assert "2 MiB" in lib.oc_status_string(rc).decode()
