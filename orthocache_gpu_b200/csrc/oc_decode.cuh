@@ -265,6 +265,13 @@ __device__ __forceinline__ void reduce_scatter(float* v, int c) {
 
 __device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
 
+// Atomic add with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // ---------------------------------------------------------------- config
 template <typename KT, typename VT, int HD, int GC, bool ATTN, int NSLOT, bool TC>
 struct Cfg {
@@ -439,17 +446,16 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     const uint32_t dst = smem_u32(ring + s * SLOT);
     const int row = isv ? CF::ROWV : CF::ROWK;
     const void* tm = isv ? static_cast<const void*>(&tmV) : static_cast<const void*>(&tmK);
-    const int* tpos = isv ? p.tm_pos_v : p.tm_pos_k;
+    const int pt = isv ? p.tm_pos_v[0] : p.tm_pos_k[0];  // tensor-map dimension of the token index
+    const int ph = isv ? p.tm_pos_v[1] : p.tm_pos_k[1];  // ... of the kv-head index
+    // coordinate of tensor-map dimension d (1..3)
+    auto crd = [&](int d, int tok, int kvh_, int outer) { return d == pt ? tok : (d == ph ? kvh_ : outer); };
     __syncwarp();
     if (p.layout == LAYOUT_LINEAR) {  // one box of 64 rows
       if (lane == 0) {
         mbar_arrive_expect_tx(fbar, 64u * row / P);
-        int cc[4];
-        cc[0] = panel * 64;
-        cc[tpos[0]] = tile * 64;
-        cc[tpos[1]] = kvh;
-        cc[tpos[2]] = seq;
-        tma_load_4d(dst, tm, cc[0], cc[1], cc[2], cc[3], fbar, pol);
+        tma_load_4d(dst, tm, panel * 64, crd(1, tile * 64, kvh, seq), crd(2, tile * 64, kvh, seq),
+                    crd(3, tile * 64, kvh, seq), fbar, pol);
       }
       return;
     }
@@ -464,12 +470,9 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         atomicOr(p.status, ST_BAD_PAGE);
         pb = 0;
       }
-      int cc[4];
-      cc[0] = panel * 64;
-      cc[tpos[0]] = t & ((1 << p.block_shift) - 1);
-      cc[tpos[1]] = kvh;
-      cc[tpos[2]] = pb;
-      tma_load_4d(dst + (uint32_t)(run * RB * (row / P)), tm, cc[0], cc[1], cc[2], cc[3], fbar, pol);
+      const int tk = t & ((1 << p.block_shift) - 1);
+      tma_load_4d(dst + (uint32_t)(run * RB * (row / P)), tm, panel * 64, crd(1, tk, kvh, pb), crd(2, tk, kvh, pb),
+                  crd(3, tk, kvh, pb), fbar, pol);
     }
   };
 
@@ -691,38 +694,47 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
           }
       }
       if (direct) return;
-      __threadfence();
+      // ticket: release this warp's partial, and the last of the unit's teams
+      // acquires all of them (lanes' stores are ordered by the warp barrier)
       __syncwarp();
       int last = 0;
       uint32_t* ticket = p.tickets + (int64_t)u * P + panel;  // one merge per (unit, panel)
-      if (lane == 0) last = (atomicAdd(ticket, 1u) == (uint32_t)(w1 - w0)) ? 1 : 0;
+      if (lane == 0) last = (atom_add_acq_rel_gpu(ticket, 1u) == (uint32_t)(w1 - w0)) ? 1 : 0;
       last = __shfl_sync(0xffffffffu, last, 0);
       if (!last) return;
-      __threadfence();
+      __syncwarp();
       if (lane == 0) *ticket = 0u;
+      const int n = (int)(w1 - w0 + 1);
+      const int64_t sl0 = partial_slot(w0, R0, N, WE);
+      auto slot_i = [&](int i) -> int64_t { return i == 0 ? sl0 : 2 * (w0 + i); };
       constexpr int NE = (HDL + 31) / 32;  // columns per lane in the merge
       for (int g = 0; g < gvalid; ++g) {
+        // (m, l) of the partials lane-parallel, then the accumulators with independent loads
         float M = -INFINITY;
-        for (int64_t w = w0 + lane; w <= w1; w += 32) {
-          const int64_t sl = (w == w0) ? partial_slot(w0, R0, N, WE) : 2 * w;
-          M = fmaxf(M, __ldcg(rec_of(sl, g) + HDL));
-        }
+        for (int i = lane; i < n; i += 32) M = fmaxf(M, __ldcg(rec_of(slot_i(i), g) + HDL));
         M = warp_max(M);
         float lt = 0.f;
         float a[NE];
 #pragma unroll
         for (int e = 0; e < NE; ++e) a[e] = 0.f;
-#pragma unroll 4
-        for (int64_t w = w0; w <= w1; ++w) {
-          const int64_t sl = (w == w0) ? partial_slot(w0, R0, N, WE) : 2 * w;
-          const float* rec = rec_of(sl, g);
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec + HDL));
-          const float wt = exp2f(ml.x - M);
-          lt = fmaf(ml.y, wt, lt);
+        for (int b0 = 0; b0 < n; b0 += 32) {
+          float wt = 0.f;
+          if (b0 + lane < n) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec_of(slot_i(b0 + lane), g) + HDL));
+            wt = exp2f(ml.x - M);
+            lt = fmaf(ml.y, wt, lt);
+          }
+          const int cnt = n - b0 < 32 ? n - b0 : 32;
+#pragma unroll 8
+          for (int k = 0; k < cnt; ++k) {
+            const float w = __shfl_sync(0xffffffffu, wt, k);
+            const float* rec = rec_of(slot_i(b0 + k), g);
 #pragma unroll
-          for (int e = 0; e < NE; ++e)
-            if (lane + 32 * e < HDL) a[e] = fmaf(__ldcg(rec + lane + 32 * e), wt, a[e]);
+            for (int e = 0; e < NE; ++e)
+              if (lane + 32 * e < HDL) a[e] = fmaf(__ldcg(rec + lane + 32 * e), w, a[e]);
+          }
         }
+        lt = warp_sum(lt);
 #pragma unroll
         for (int e = 0; e < NE; ++e)
           if (lane + 32 * e < HDL)
@@ -736,6 +748,22 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   float2 qv[TC ? 1 : GC][D2];
   uint32_t qf[TC ? HDL / 16 : 1][2];  // q (this warp's panel) as mma B fragments (dims x queries), raw 16-bit
   int q_unit = -1;
+  uint32_t qf_pf[TC ? HDL / 16 : 1][2];  // prefetched fragments of unit pf_unit
+  int pf_unit = -1;
+  // q rows of a unit's query chunk (this warp's panel) as raw 16-bit mma B fragments
+  auto load_qf = [&](int seq, int kvh, int chunk, uint32_t (&dst)[TC ? HDL / 16 : 1][2]) {
+    if constexpr (TC) {
+      const int hq = chunk * GC + g8;
+      const bool ok = g8 < GC && hq < p.group;
+      const uint16_t* qrow = static_cast<const uint16_t*>(p.q) + (int64_t)seq * p.q_seq_stride +
+                             (int64_t)(kvh * p.group + hq) * p.q_head_stride + panel * HDL;
+#pragma unroll
+      for (int ks = 0; ks < HDL / 16; ++ks) {
+        dst[ks][0] = ok ? (uint32_t)qrow[16 * ks + 2 * t4] | ((uint32_t)qrow[16 * ks + 2 * t4 + 1] << 16) : 0u;
+        dst[ks][1] = ok ? (uint32_t)qrow[16 * ks + 2 * t4 + 8] | ((uint32_t)qrow[16 * ks + 2 * t4 + 9] << 16) : 0u;
+      }
+    }
+  };
 
   // descriptor of ring slot `lane` (lanes < NSLOT): flattened tile (-1: empty),
   // V copy flag, unit and tile index
@@ -749,6 +777,10 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     u_iss = u;
     seq_iss = unit_seq(u);
     kvh_iss = unit_kvh(u);
+    if constexpr (ATTN && TC) {
+      load_qf(seq_iss, kvh_iss, unit_chunk(u), qf_pf);
+      pf_unit = u;
+    }
     it_iss.init((int)(f - tp[u]), tp[u + 1] - tp[u], S);
   };
   if (fb > fa) enter_unit(u_first, fa);
@@ -814,14 +846,14 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
           const int seq = seq_k, kvh = kvh_k, chunk = chunk_k;
           const int64_t qb = (int64_t)seq * p.q_seq_stride;
           if constexpr (TC) {
-            const int hq = chunk * GC + g8;
-            const bool ok = g8 < GC && hq < p.group;
-            const uint16_t* qrow = static_cast<const uint16_t*>(p.q) + qb +
-                                   (int64_t)(kvh * p.group + hq) * p.q_head_stride + panel * HDL;
+            if (u == pf_unit) {  // fragments prefetched when the copy cursor entered the unit
 #pragma unroll
-            for (int ks = 0; ks < HDL / 16; ++ks) {
-              qf[ks][0] = ok ? (uint32_t)qrow[16 * ks + 2 * t4] | ((uint32_t)qrow[16 * ks + 2 * t4 + 1] << 16) : 0u;
-              qf[ks][1] = ok ? (uint32_t)qrow[16 * ks + 2 * t4 + 8] | ((uint32_t)qrow[16 * ks + 2 * t4 + 9] << 16) : 0u;
+              for (int ks = 0; ks < HDL / 16; ++ks) {
+                qf[ks][0] = qf_pf[ks][0];
+                qf[ks][1] = qf_pf[ks][1];
+              }
+            } else {
+              load_qf(seq, kvh, chunk, qf);
             }
           } else {
 #pragma unroll
@@ -836,7 +868,30 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
                               : make_float2(0.f, 0.f);
             }
           }
-          if (p.gate == GATE_CS) {
+          if (p.gate == GATE_CS && p.group <= 8) {
+            // max_g |q_g|: four lanes per query head, one round of independent loads
+            const int g = lane >> 2, part = lane & 3;
+            float ss = 0.f;
+            if (g < p.group) {
+              const int64_t row = qb + (int64_t)(kvh * p.group + g) * p.q_head_stride + part * (HD / 4);
+#pragma unroll 8
+              for (int d = 0; d < HD / 4; ++d) {
+                const float x = load_any(p.q, row + d, p.q_dtype);
+                ss = fmaf(x, x, ss);
+              }
+            }
+            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+            float qn = sqrtf(ss);
+            if (qn < 1e-38f) qn = 0.f;
+            if (g >= p.group) qn = 0.f;
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {  // max over the heads; a NaN norm propagates like torch.max
+              const float y = __shfl_xor_sync(0xffffffffu, qn, o);
+              qn = (qn != qn || y != y) ? __int_as_float(0x7fc00000) : fmaxf(qn, y);
+            }
+            qmax = qn;
+          } else if (p.gate == GATE_CS) {
             qmax = 0.f;
             for (int g = 0; g < p.group; ++g) {
               const int64_t row = qb + (int64_t)(kvh * p.group + g) * p.q_head_stride;
