@@ -175,8 +175,8 @@ int sms_or_device(int num_sms) {
 }
 
 // Workspace layout (every region 256-byte aligned):
-//   fixed header (kFixedBytes, zero between launches): merge tickets, one per
-//     (unit, 64-column panel), at most 4 panels a unit
+//   fixed header (kFixedBytes): the per-unit tile prefix for the merge
+//     kernel (written by every launch; sized for 4 ints a unit)
 //   part  partial states, 2 slots per team of warps: 2*kMaxWarps*gc*(hd+16) f32
 constexpr int64_t kMaxUnits = 2048;  // units per launch (shared-memory prefix arrays)
 constexpr int64_t kMaxWarps = 1280;
@@ -199,7 +199,7 @@ int attach_workspace(DecodeParams& p, int64_t units, int hd, void* ws, size_t ws
   const WsLayout L = ws_layout(units, gc, p.num_tiles, hd);
   if (ws == nullptr || ws_bytes < L.total || !aligned16(ws)) return OC_ERR_WORKSPACE;
   char* b = static_cast<char*>(ws);
-  p.tickets = reinterpret_cast<uint32_t*>(b);
+  p.tile_prefix = reinterpret_cast<int*>(b);
   p.part = reinterpret_cast<float*>(b + L.part);
   return OC_OK;
 }

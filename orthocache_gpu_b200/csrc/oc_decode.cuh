@@ -119,8 +119,8 @@ struct DecodeParams {
   float* score;       // same shape: zeta or Cauchy-Schwarz bound, nullable
   uint32_t* stats;    // [0] += retained tiles, nullable
   uint32_t* status;   // error bits, non-null
-  // workspace (attention only); tickets are zero between launches
-  uint32_t* tickets;   // merge tickets per (unit, panel)
+  // workspace (attention only)
+  int* tile_prefix;    // tiles of units [0, u): written by CTA 0 for merge_kernel (units + 1 ints)
   float* part;         // partial states [2 * teams][GC][P][HD/P + 4]: acc, m, l
   // shard mode (nullable): write the merged partial state (m, l, unnormalised
   // acc) of each query head instead of the normalised output
@@ -265,13 +265,6 @@ __device__ __forceinline__ void reduce_scatter(float* v, int c) {
 
 __device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
 
-// Atomic add with acquire-release semantics at GPU scope; returns the old value.
-__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
-
 // ---------------------------------------------------------------- config
 template <typename KT, typename VT, int HD, int GC, bool ATTN, int NSLOT, bool TC>
 struct Cfg {
@@ -406,6 +399,8 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   }
   block_scan(tp, U, scan_tmp);
   const int64_t N = tp[U];
+  if (ATTN && blockIdx.x == 0)
+    for (int u = tid; u <= U; u += blockDim.x) p.tile_prefix[u] = tp[u];
 
   const uint64_t pol = policy_evict_first();
 
@@ -479,7 +474,10 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // Wait for the copy in slot s (bounded; a timeout sets the status bit).
   uint32_t phases = 0;  // bit s: parity of slot s's next completion
 #ifdef OC_PROBE_WAIT
-  long long pw_wait = 0, pw_t0 = clock64(), pw_gate = 0, pw_iss = 0;
+  long long pw_wait = 0, pw_t0 = clock64(), pw_gate = 0, pw_iss = 0, pw_first = 0, pw_fin = 0, pw_fa = 0, pw_fm = 0, pw_kc = 0, pw_vc = 0;
+  int pw_kn = 0, pw_vn = 0;
+  unsigned long long pw_g0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(pw_g0));
   int pw_n = 0;
 #endif
   auto wait_slot = [&](uint32_t s) {
@@ -491,6 +489,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     phases ^= 1u << s;
 #ifdef OC_PROBE_WAIT
     pw_wait += clock64() - a0;
+    if (pw_n == 0) pw_first = clock64() - pw_t0;
     ++pw_n;
 #endif
     __syncwarp();
@@ -693,53 +692,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
                   empty ? make_float2(-1e9f, 0.f) : make_float2(m_run[g], lsum[g]);
           }
       }
-      if (direct) return;
-      // ticket: release this warp's partial, and the last of the unit's teams
-      // acquires all of them (lanes' stores are ordered by the warp barrier)
-      __syncwarp();
-      int last = 0;
-      uint32_t* ticket = p.tickets + (int64_t)u * P + panel;  // one merge per (unit, panel)
-      if (lane == 0) last = (atom_add_acq_rel_gpu(ticket, 1u) == (uint32_t)(w1 - w0)) ? 1 : 0;
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) return;
-      __syncwarp();
-      if (lane == 0) *ticket = 0u;
-      const int n = (int)(w1 - w0 + 1);
-      const int64_t sl0 = partial_slot(w0, R0, N, WE);
-      auto slot_i = [&](int i) -> int64_t { return i == 0 ? sl0 : 2 * (w0 + i); };
-      constexpr int NE = (HDL + 31) / 32;  // columns per lane in the merge
-      for (int g = 0; g < gvalid; ++g) {
-        // (m, l) of the partials lane-parallel, then the accumulators with independent loads
-        float M = -INFINITY;
-        for (int i = lane; i < n; i += 32) M = fmaxf(M, __ldcg(rec_of(slot_i(i), g) + HDL));
-        M = warp_max(M);
-        float lt = 0.f;
-        float a[NE];
-#pragma unroll
-        for (int e = 0; e < NE; ++e) a[e] = 0.f;
-        for (int b0 = 0; b0 < n; b0 += 32) {
-          float wt = 0.f;
-          if (b0 + lane < n) {
-            const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec_of(slot_i(b0 + lane), g) + HDL));
-            wt = exp2f(ml.x - M);
-            lt = fmaf(ml.y, wt, lt);
-          }
-          const int cnt = n - b0 < 32 ? n - b0 : 32;
-#pragma unroll 8
-          for (int k = 0; k < cnt; ++k) {
-            const float w = __shfl_sync(0xffffffffu, wt, k);
-            const float* rec = rec_of(slot_i(b0 + k), g);
-#pragma unroll
-            for (int e = 0; e < NE; ++e)
-              if (lane + 32 * e < HDL) a[e] = fmaf(__ldcg(rec + lane + 32 * e), w, a[e]);
-          }
-        }
-        lt = warp_sum(lt);
-#pragma unroll
-        for (int e = 0; e < NE; ++e)
-          if (lane + 32 * e < HDL)
-            emit(p, seq, kvh * p.group + chunk * GC + g, panel * HDL + lane + 32 * e, M, lt, a[e]);
-      }
+      // split units are merged by merge_kernel once the grid has completed
     };
 
 
@@ -830,6 +783,9 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       continue;
     }
     unsigned char* ts = wait_slot(s);
+#ifdef OC_PROBE_WAIT
+    const long long it0 = clock64();
+#endif
     float* lgs = lgs_base + s * (CF::LGB / 4);
     if (!isv) {
       // ================================================ K tile: gate (+ logits)
@@ -1078,7 +1034,13 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       }
       if constexpr (ATTN) {
         const int64_t uend = tp[u + 1] < fb ? tp[u + 1] : fb;
+#ifdef OC_PROBE_WAIT
+        const long long f0 = clock64();
+#endif
         if (f + 1 == uend && kept_k == 0) finalize(u, true);
+#ifdef OC_PROBE_WAIT
+        pw_fin += clock64() - f0;
+#endif
       }
     } else {
       // ================================================ V tile of a retained tile
@@ -1211,12 +1173,21 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       __syncwarp();
       issue_next(s);
     }
+#ifdef OC_PROBE_WAIT
+    if (isv) { pw_vc += clock64() - it0; ++pw_vn; } else { pw_kc += clock64() - it0; ++pw_kn; }
+#endif
     if constexpr (ATTN) {
       if (acc_unit >= 0) {
         const int64_t ua = tp[acc_unit], uend = tp[acc_unit + 1] < fb ? tp[acc_unit + 1] : fb;
         if (f_gated >= uend &&
             !__any_sync(0xffffffffu, lane < NSLOT && dsc_f >= ua && dsc_f < uend && dsc_v != 0)) {
+#ifdef OC_PROBE_WAIT
+          const long long f0 = clock64();
+#endif
           finalize(acc_unit, false);
+#ifdef OC_PROBE_WAIT
+          pw_fin += clock64() - f0;
+#endif
           acc_unit = -1;
           reset_state();
         }
@@ -1224,11 +1195,101 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     }
   }
   if (p.stats && lane == 0 && kept_stat) atomicAdd(p.stats, (uint32_t)kept_stat);
+  // this CTA's decode work is issued: the merge grid may be scheduled (its
+  // griddepcontrol.wait still waits for the whole grid to complete)
+  if constexpr (ATTN) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 #ifdef OC_PROBE_WAIT
-  if (lane == 0 && (blockIdx.x % 50 == 0))
-    printf("PW blk %d w %d items %d cyc/item %lld wait %lld gate %lld issue %lld\n", blockIdx.x, warp, pw_n,
-           (clock64() - pw_t0) / (pw_n ? pw_n : 1), pw_wait / (pw_n ? pw_n : 1), pw_gate / (pw_n ? pw_n : 1), pw_iss / (pw_n ? pw_n : 1));
+  unsigned long long pw_g1;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(pw_g1));
+  if (lane == 0 && warp == 0)
+    printf("PW blk %d w %d items %d total %lld first %lld fin %lld K %lld x%d V %lld x%d cyc/item %lld wait %lld gate %lld issue %lld g0 %llu ns %llu\n",
+           blockIdx.x, warp, pw_n, clock64() - pw_t0, pw_first, pw_fin, pw_kc / (pw_kn ? pw_kn : 1), pw_kn, pw_vc / (pw_vn ? pw_vn : 1), pw_vn, (clock64() - pw_t0) / (pw_n ? pw_n : 1),
+           pw_wait / (pw_n ? pw_n : 1), pw_gate / (pw_n ? pw_n : 1), pw_iss / (pw_n ? pw_n : 1), pw_g0 % 1000000000ull, pw_g1 - pw_g0);
 #endif
+}
+
+// Merge of the units that several teams share, launched as a programmatic
+// dependent of decode_kernel: griddepcontrol.wait returns once the decode
+// grid has completed and its stores are visible, so the partial states need
+// no fences or tickets.  One warp per (unit, 64-column panel) combines the
+// unit's partial states (log-sum-exp: running max M, weights 2^(m - M)) and
+// writes the output; units held whole by one team were written directly.
+template <int HD, int GC, int P>
+__global__ void __launch_bounds__(128) merge_kernel(const DecodeParams p, int64_t W) {
+  constexpr int HDL = HD / P, PST = HDL + 4;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int nchunks = (p.group + GC - 1) / GC;
+  const int U = p.num_seqs * p.num_kv_heads * nchunks;
+  if (item >= (int64_t)U * P) return;
+  const int u = (int)(item / P), panel = (int)(item % P);
+  const int* tp = p.tile_prefix;
+  const int64_t N = tp[U];
+  const int64_t WE = (N < W) ? (N > 0 ? N : 1) : W;
+  const int64_t R0 = tp[u], R1 = (int64_t)tp[u + 1] - 1;
+  if (R1 < R0) return;  // a unit without tiles was written by the decode kernel
+  const int64_t w0 = range_owner(R0, N, WE), w1 = range_owner(R1, N, WE);
+  if (w0 == w1) return;
+  const int seq = u / (p.num_kv_heads * nchunks), kvh = (u / nchunks) % p.num_kv_heads, chunk = u % nchunks;
+  const int gvalid = (p.group - chunk * GC) < GC ? (p.group - chunk * GC) : GC;
+  auto rec_of = [&](int64_t sl, int g) -> const float* { return p.part + ((sl * GC + g) * P + panel) * PST; };
+  const int n = (int)(w1 - w0 + 1);
+  const int64_t sl0 = partial_slot(w0, R0, N, WE);
+  auto slot_i = [&](int i) -> int64_t { return i == 0 ? sl0 : 2 * (w0 + i); };
+  constexpr int NE = (HDL + 31) / 32;  // columns per lane
+  constexpr int CH = NE <= 2 ? 16 : (NE <= 4 ? 8 : 4);  // partials whose accumulators are loaded together
+      for (int g = 0; g < gvalid; ++g) {
+        // (m, l) of partial `lane` and the accumulators of the first CH partials
+        // are loaded in the same round; M over all partials.
+        float mi = -INFINITY, li = 0.f;
+        if (lane < n) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec_of(slot_i(lane), g) + HDL));
+          mi = ml.x;
+          li = ml.y;
+        }
+        float a[NE];
+#pragma unroll
+        for (int e = 0; e < NE; ++e) a[e] = 0.f;
+        float lt = 0.f, M = -INFINITY;
+        for (int b0 = 0; b0 < n; b0 += CH) {
+          float v[CH][NE];
+#pragma unroll
+          for (int k = 0; k < CH; ++k)
+#pragma unroll
+            for (int e = 0; e < NE; ++e)
+              v[k][e] = (b0 + k < n && lane + 32 * e < HDL) ? __ldcg(rec_of(slot_i(b0 + k), g) + lane + 32 * e) : 0.f;
+          if (b0 == 0) {
+            M = mi;
+            for (int i = lane + 32; i < n; i += 32) M = fmaxf(M, __ldcg(rec_of(slot_i(i), g) + HDL));
+            M = warp_max(M);
+          }
+          // weights of partials b0 .. b0+CH-1 (lanes hold partials 32 j + lane)
+          const int base32 = b0 & ~31;
+          float wt = 0.f;
+          if (base32 + lane < n) {
+            float mm = mi, ll = li;
+            if (base32 > 0) {
+              const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec_of(slot_i(base32 + lane), g) + HDL));
+              mm = ml.x;
+              ll = ml.y;
+            }
+            wt = exp2f(mm - M);
+            if (b0 == base32) lt = fmaf(ll, wt, lt);
+          }
+#pragma unroll
+          for (int k = 0; k < CH; ++k) {
+            const float w = __shfl_sync(0xffffffffu, wt, (b0 - base32 + k) & 31);
+#pragma unroll
+            for (int e = 0; e < NE; ++e) a[e] = fmaf(v[k][e], w, a[e]);
+          }
+        }
+        lt = warp_sum(lt);
+#pragma unroll
+        for (int e = 0; e < NE; ++e)
+          if (lane + 32 * e < HDL)
+            emit(p, seq, kvh * p.group + chunk * GC + g, panel * HDL + lane + 32 * e, M, lt, a[e]);
+      }
 }
 
 template <typename KT, typename VT, int HD, int GC, bool ATTN, int NSLOT, bool TC>
@@ -1254,7 +1315,11 @@ cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tk, const CU
   // about two tiles per team, at most one wave of resident CTAs
   constexpr int kTeams = CF::NW / CF::P;
   const int64_t want = (tiles + 2 * kTeams - 1) / (2 * kTeams);
-  const int64_t cap = (int64_t)num_sms * resident[dev];
+  // at most one wave of resident CTAs on this device, whatever num_sms says
+  static int dev_sms[64] = {0};
+  if (dev_sms[dev] == 0) cudaDeviceGetAttribute(&dev_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int sms_cap = (num_sms > 0 && num_sms < dev_sms[dev]) ? num_sms : dev_sms[dev];
+  const int64_t cap = (int64_t)sms_cap * resident[dev];
   int64_t grid = want < 1 ? 1 : (want > cap ? cap : want);
   if (grid * CF::NW > CF::MAXW) grid = CF::MAXW / CF::NW;
   cudaLaunchConfig_t cfg = {};
@@ -1263,7 +1328,21 @@ cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tk, const CU
   cfg.dynamicSmemBytes = CF::SMEM;
   cfg.stream = stream;
   cfg.numAttrs = 0;
-  return cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
+  if (e != cudaSuccess || !ATTN) return e;
+  // merge of the units shared by several teams: a programmatic dependent launch
+  constexpr int kMergeWarps = 4;
+  const int64_t items = (int64_t)p.num_seqs * p.num_kv_heads * nchunks * CF::P;
+  cudaLaunchConfig_t mc = {};
+  mc.gridDim = dim3((unsigned)((items + kMergeWarps - 1) / kMergeWarps));
+  mc.blockDim = dim3(32 * kMergeWarps);
+  mc.stream = stream;
+  cudaLaunchAttribute ma[1];
+  ma[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  ma[0].val.programmaticStreamSerializationAllowed = 1;
+  mc.attrs = ma;
+  mc.numAttrs = 1;
+  return cudaLaunchKernelEx(&mc, merge_kernel<HD, GC, CF::P>, p, grid * (int64_t)(CF::NW / CF::P));
 }
 
 }  // namespace oc
