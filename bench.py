@@ -174,6 +174,97 @@ def graph_of(fn, n):
     return g
 
 
+def _mixture_device(lead, seq, hd, g, dev):
+    """Tile mixture (as mha_inputs_device) for keys of shape lead + (seq, hd), float32 on dev."""
+    from orthocache_gpu_b200.synthetic import walsh
+    n = int(np.prod(lead)) * (seq // 64)
+    keys = torch.randn((n, 64, hd), generator=g, device=dev)
+    smooth = torch.rand(n, generator=g, device=dev) < 0.5
+    w8 = torch.from_numpy(walsh(64)[:, :8]).to(dev)
+    sm = torch.matmul(w8, torch.randn((n, 8, hd), generator=g, device=dev)) + \
+        0.05 * torch.randn(keys.shape, generator=g, device=dev)
+    return torch.where(smooth[:, None, None], sm, keys).reshape(*lead, seq, hd)
+
+
+def _zero_high_half(q):
+    """Device version of synthetic.zero_high_band_queries (every other head, rows [hd/2, hd))."""
+    from orthocache_gpu_b200.synthetic import walsh
+    hd = q.shape[-1]
+    w = torch.from_numpy(walsh(hd)).to(q.device)
+    spec = q @ w.T
+    spec[..., 1::2, hd // 2:] = 0.0
+    return spec @ w
+
+
+def _graph_us(fn, n=20, reps=5):
+    g = graph_of(lambda i=0: fn(), n)
+    return time_fn(g.replay, reps) / n
+
+
+def extra_configs(dev):
+    """The reference's other measured configurations, timed on one GPU (graph-replayed).
+
+    Config 3: V3 Cauchy-Schwarz GQA, batch 16, 32 query / 8 kv heads, hd 128,
+    32K tokens, bf16, half of the query heads with their high band zeroed,
+    tau 150 (about half the tiles evicted).  Config 4: paged GQA, 64
+    sequences of U[2K, 64K] tokens (multiples of 64), 16-token pages in a
+    permuted pool, 32 / 8 heads, hd 128, fp16, Cauchy-Schwarz gate tau 150.
+    Bytes = all K tiles + retained V tiles (+ q, out).  Inputs are larger than L2.
+    """
+    import orthocache_gpu_b200 as oc
+    out = []
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    B, KVH, G, S, HD, TAU = 16, 8, 4, 32768, 128, 150.0
+    k = _mixture_device((B, KVH), S, HD, g, dev).to(torch.bfloat16)
+    v = torch.randn(k.shape, generator=g, device=dev).to(torch.bfloat16)
+    q = _zero_high_half(torch.randn((B, KVH * G, HD), generator=g, device=dev)).to(torch.bfloat16)
+    kept = oc.fused_orthocache_attention_v3_gqa(q, k, v, TAU, G)[1]["tiles_retained"]
+    us = _graph_us(lambda: oc.fused_orthocache_attention_v3_gqa(q, k, v, TAU, G, stats=False))
+    nt = B * KVH * (S // 64)
+    nb = nt * 64 * HD * 2 + kept * 64 * HD * 2
+    out.append({"config": "V3 GQA batch 16, 32Q/8KV, hd 128, 32K, bf16, tau 150", "us": round(us, 2),
+                "gbs": round(nb / (us * 1e-6) / 1e9, 1), "evict": round(1 - kept / nt, 3),
+                "algorithmic_bytes": int(nb)})
+    del k, v, q
+    torch.cuda.empty_cache()
+
+    rng = np.random.default_rng(0)
+    NS, BS = 64, 16
+    lens = rng.integers(2048, 65536 + 1, size=NS)
+    lens = (lens - lens % 64).astype(np.int64)
+    nblk = lens // BS
+    total = int(nblk.sum())
+    perm = torch.from_numpy(rng.permutation(total).astype(np.int64)).to(dev)
+    kc = torch.empty((total, KVH, BS, HD), dtype=torch.float16, device=dev)
+    vc = torch.empty_like(kc)
+    tables = torch.zeros((NS, int(nblk.max())), dtype=torch.int32, device=dev)
+    pos = 0
+    for s_ in range(NS):
+        L, nb_ = int(lens[s_]), int(nblk[s_])
+        pages = perm[pos:pos + nb_]
+        pos += nb_
+        ks = _mixture_device((KVH,), L, HD, g, dev)
+        kc[pages] = ks.reshape(KVH, nb_, BS, HD).permute(1, 0, 2, 3).to(torch.float16)
+        vc[pages] = torch.randn((nb_, KVH, BS, HD), generator=g, device=dev).to(torch.float16)
+        tables[s_, :nb_] = pages.to(torch.int32)
+        tables[s_, nb_:] = pages[0].to(torch.int32)
+        del ks
+    seq_lens = torch.from_numpy(lens.astype(np.int32)).to(dev)
+    qp = _zero_high_half(torch.randn((NS, KVH * G, HD), generator=g, device=dev)).to(torch.float16)
+    kw = dict(tau=TAU, seq_lens=seq_lens)
+    kept = oc.fused_orthocache_attention_paged(qp, kc, vc, tables, None, **kw)[1]["tiles_retained"]
+    us = _graph_us(lambda: oc.fused_orthocache_attention_paged(qp, kc, vc, tables, None, stats=False, **kw))
+    nt = int((lens // 64).sum()) * KVH
+    nb = nt * 64 * HD * 2 + kept * 64 * HD * 2
+    out.append({"config": "paged GQA, 64 seqs U[2K,64K], page 16, 32Q/8KV, hd 128, fp16, tau 150",
+                "us": round(us, 2), "gbs": round(nb / (us * 1e-6) / 1e9, 1), "evict": round(1 - kept / nt, 3),
+                "algorithmic_bytes": int(nb)})
+    del kc, vc, qp
+    torch.cuda.empty_cache()
+    return out
+
+
 def cpu_baseline(seq, sample_heads=8, min_seconds=10.0):
     """Oracle (NumPy restatement of the reference CPU path) on a bounded sample.
 
@@ -342,6 +433,7 @@ def main():
             if sl != seq:
                 del qs, ks, vs
         extra["sweep"] = sweep
+        extra["configs"] = extra_configs(dev)
 
     if rank == 0:
         cb = cpu_baseline(seq, a.cpu_sample_heads or 8)
@@ -359,7 +451,7 @@ def main():
                          "launch_us": round(launch_us, 3)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": steps,
+            "gpu_launches": 2 * steps,  # decode kernel + split-unit merge kernel per call
             "clocks": clk.summary(),
             "cpu_baseline": cb,
             **extra,
