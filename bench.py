@@ -262,6 +262,20 @@ def extra_configs(dev):
                 "algorithmic_bytes": int(nb)})
     del kc, vc, qp
     torch.cuda.empty_cache()
+
+    # config 5b: TinyLlama-1.1B-shaped random-init model, 16K random-token prompt,
+    # 256 greedy steps, fused gate in every layer (median-calibrated tau) vs dense SDPA
+    from orthocache_gpu_b200.model import GatedLlama, LlamaShape
+    m = GatedLlama(LlamaShape(), max_len=16384 + 320, device=dev, seed=5)
+    prompt = torch.randint(0, 32000, (16384,), generator=g, device=dev)
+    row = {"config": "TinyLlama-1.1B-shaped random-init, 22 layers, 32Q/4KV, hd 64, bf16, 16K prompt, "
+                     "256 greedy steps (eager per-step device time, median)"}
+    for mode, key in (("median", "fused_ms_per_token"), (None, "dense_sdpa_ms_per_token")):
+        r = m.generate(prompt, 256, tau_mode=mode)
+        row[key] = round(r["ms_per_token"], 3)
+    out.append(row)
+    del m
+    torch.cuda.empty_cache()
     return out
 
 

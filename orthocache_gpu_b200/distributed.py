@@ -42,11 +42,12 @@ def shard_range(seq_len: int, world_size: int, rank: int, tile_size: int = TILE_
 
 def shard_partials(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, tau: float,
                    num_query_groups: int, num_splits: Optional[int] = None,
-                   k_scale: float = 1.0) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, int]:
+                   k_scale: float = 1.0, stats: bool = True) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, int]:
     """This rank's merged state over its K / V shard.
 
     q (Hq, hd); keys / values (KVH, S_shard, hd).  Returns float32 tensors
-    m (Hq,), l (Hq,), acc (Hq, hd) and the number of retained tiles.
+    m (Hq,), l (Hq,), acc (Hq, hd) and the number of retained tiles (-1 with
+    ``stats=False``, which skips that host synchronisation).
     """
     num_kv_heads, seq_len, head_dim = keys.shape
     G = num_query_groups
@@ -70,15 +71,16 @@ def shard_partials(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, ta
     acc = torch.empty((hq, head_dim), dtype=torch.float32, device=dev)
     ws = _lib.workspace(dev)
     wbuf = ws.get(lib.oc_workspace_bytes(num_kv_heads, G, num_tiles, head_dim))
-    ws.ctrl[0].zero_()
+    if stats:
+        ws.ctrl[0].zero_()
     _lib.check(lib.oc_fused_attention_v3_shard(
         q.data_ptr(), _lib.dtype_code(q), q.stride(0),
         keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1),
         values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1),
         num_kv_heads, G, seq_len, head_dim, float(tau), num_splits, _lib.num_sms(dev),
-        m.data_ptr(), l.data_ptr(), acc.data_ptr(), 0, ws.ctrl.data_ptr(), ws.ctrl[1:].data_ptr(),
+        m.data_ptr(), l.data_ptr(), acc.data_ptr(), 0, ws.ctrl.data_ptr() if stats else 0, ws.ctrl[1:].data_ptr(),
         wbuf.data_ptr(), wbuf.numel(), _lib.stream_ptr(dev)), "oc_fused_attention_v3_shard")
-    return m, l, acc, _lib.read_stats(ws)
+    return m, l, acc, (_lib.read_stats(ws) if stats else -1)
 
 
 def pack_state(m: torch.Tensor, l: torch.Tensor, acc: torch.Tensor) -> torch.Tensor:

@@ -1,0 +1,198 @@
+"""A Llama-shaped decoder whose decode attention is the fused eviction kernel.
+
+The reference evaluates its gate inside HF Llama decoding (TinyLlama-1.1B,
+eval/perplexity_eval.py:693-745).  This module is the self-contained
+equivalent for measurement: random-initialised weights of the
+TinyLlama-1.1B shape (22 layers, hidden 2048, 32 query / 4 kv heads,
+head_dim 64, MLP 5632, vocab 32000, RMSNorm, rotary embeddings), a
+preallocated KV cache, dense causal prefill, and greedy decoding in which
+every layer's attention runs the Cauchy-Schwarz-gated kernel over the
+cache's whole 64-token tiles.  Tokens after the last whole tile (fewer than
+64) are attended densely and merged with the kernel's softmax state by the
+library's log-sum-exp merge, so nothing is dropped except evicted tiles.
+No pretrained weights are loaded (none are needed to measure the path).
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+import torch.nn.functional as F
+
+from .distributed import merge_states, shard_partials
+
+LOG2E = 1.4426950408889634
+
+
+@dataclass
+class LlamaShape:
+    layers: int = 22
+    hidden: int = 2048
+    heads: int = 32
+    kv_heads: int = 4
+    head_dim: int = 64
+    mlp: int = 5632
+    vocab: int = 32000
+    rope_theta: float = 10000.0
+    eps: float = 1e-5
+
+
+def _rms(x, w, eps):
+    return (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
+
+
+def _rope(x, pos, theta):
+    """Rotary embedding (rotate-half form) of x (..., T, hd) at positions pos (T,)."""
+    hd = x.shape[-1]
+    inv = theta ** (-torch.arange(0, hd, 2, device=x.device, dtype=torch.float32) / hd)
+    ang = pos.float()[:, None] * inv[None, :]
+    cos, sin = torch.cat([ang.cos(), ang.cos()], -1), torch.cat([ang.sin(), ang.sin()], -1)
+    x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
+    rot = torch.cat([-x2, x1], -1)
+    return (x.float() * cos + rot.float() * sin).to(x.dtype)
+
+
+class GatedLlama:
+    """Random-initialised Llama-shaped decoder with a preallocated KV cache.
+
+    ``tau``: a float (the Cauchy-Schwarz threshold of every layer), or
+    "median" to calibrate each layer's threshold at the first decode step as
+    the median per-tile bound max_g |q_g| |K_high|_F (about half the tiles
+    evicted), or None for dense decode attention (the reference point).
+    """
+
+    def __init__(self, shape: LlamaShape, max_len: int, device="cuda", dtype=torch.bfloat16, seed: int = 0):
+        self.s, self.dev, self.dtype, self.max_len = shape, torch.device(device), dtype, max_len
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(seed)
+
+        def w(*shape_, std=0.02):
+            return (torch.randn(*shape_, generator=g, device=self.dev) * std).to(dtype)
+
+        s = shape
+        ones = lambda n: torch.ones(n, device=self.dev, dtype=dtype)  # noqa: E731
+        self.embed = w(s.vocab, s.hidden)
+        self.layers = [dict(ln1=ones(s.hidden), wq=w(s.hidden, s.heads * s.head_dim),
+                            wk=w(s.hidden, s.kv_heads * s.head_dim), wv=w(s.hidden, s.kv_heads * s.head_dim),
+                            wo=w(s.heads * s.head_dim, s.hidden), ln2=ones(s.hidden),
+                            w1=w(s.hidden, s.mlp), w3=w(s.hidden, s.mlp), w2=w(s.mlp, s.hidden))
+                       for _ in range(s.layers)]
+        self.norm = ones(s.hidden)
+        self.lm_head = w(s.hidden, s.vocab)
+        self.k_cache = [torch.zeros(s.kv_heads, max_len, s.head_dim, device=self.dev, dtype=dtype)
+                        for _ in range(s.layers)]
+        self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
+        self.length = 0
+        self.tau: List[Optional[float]] = [None] * s.layers
+        self.kept = 0
+        self.tiles = 0
+
+    # ---------------------------------------------------------------- blocks
+    def _qkv(self, L, h, pos):
+        s = self.s
+        T = h.shape[0]
+        q = (h @ L["wq"]).view(T, s.heads, s.head_dim).transpose(0, 1)
+        k = (h @ L["wk"]).view(T, s.kv_heads, s.head_dim).transpose(0, 1)
+        v = (h @ L["wv"]).view(T, s.kv_heads, s.head_dim).transpose(0, 1)
+        return _rope(q, pos, s.rope_theta), _rope(k, pos, s.rope_theta), v
+
+    def _mlp(self, L, x):
+        h = _rms(x, L["ln2"], self.s.eps)
+        return x + (F.silu(h @ L["w1"]) * (h @ L["w3"])) @ L["w2"]
+
+    @torch.no_grad()
+    def prefill(self, tokens: torch.Tensor) -> torch.Tensor:
+        """Dense causal attention over the prompt; fills the cache; returns last-position logits."""
+        s = self.s
+        T = tokens.shape[0]
+        pos = torch.arange(T, device=self.dev)
+        x = self.embed[tokens]
+        for i, L in enumerate(self.layers):
+            q, k, v = self._qkv(L, _rms(x, L["ln1"], s.eps), pos)
+            self.k_cache[i][:, :T] = k
+            self.v_cache[i][:, :T] = v
+            a = F.scaled_dot_product_attention(q[None], k[None], v[None], is_causal=True, enable_gqa=True)[0]
+            x = x + a.transpose(0, 1).reshape(T, -1) @ L["wo"]
+            x = self._mlp(L, x)
+        self.length = T
+        return _rms(x[-1:], self.norm, s.eps) @ self.lm_head
+
+    # ---------------------------------------------------------------- decode
+    def _median_bound(self, q, k_tiles):
+        """Median over (kv head, tile) of max_g |q_g| * |K_high|_F (the gate's bound, in torch)."""
+        s = self.s
+        G = s.heads // s.kv_heads
+        kt = k_tiles.float().view(s.kv_heads, -1, 64, s.head_dim)
+        e_high = 0.5 * (kt[:, :, :32] - kt[:, :, 32:]).pow(2).sum((-1, -2))      # (KVH, T)
+        qn = q.float().view(s.kv_heads, G, s.head_dim).norm(dim=-1).amax(-1)      # (KVH,)
+        return float((qn[:, None] * e_high.sqrt()).median())
+
+    def _attend(self, i, q, tau_mode):
+        """Decode attention of layer i for q (Hq, hd) over the cache [0, length)."""
+        s = self.s
+        G = s.heads // s.kv_heads
+        n = self.length
+        full = n - n % 64
+        kc, vc = self.k_cache[i], self.v_cache[i]
+        scale = LOG2E / math.sqrt(s.head_dim)
+        if tau_mode is None or full == 0:  # dense (reference point, or no whole tile yet)
+            a = F.scaled_dot_product_attention(q[None, :, None], kc[None, :, :n], vc[None, :, :n], enable_gqa=True)
+            return a[0, :, 0]
+        if self.tau[i] is None:
+            self.tau[i] = self._median_bound(q, kc[:, :full]) if tau_mode == "median" else float(tau_mode)
+        m, l, acc, _ = shard_partials(q, kc[:, :full], vc[:, :full], self.tau[i], G, stats=False)
+        ms, ls, accs = [m], [l], [acc]
+        if n > full:  # ragged tail: dense, as a second softmax state in log2 units
+            kt = kc[:, full:n].repeat_interleave(G, 0).float()
+            vt = vc[:, full:n].repeat_interleave(G, 0).float()
+            sc = (kt @ q.float()[:, :, None])[..., 0] * scale            # (Hq, r)
+            mt = sc.amax(-1)
+            pt = torch.exp2(sc - mt[:, None])
+            ms.append(mt)
+            ls.append(pt.sum(-1))
+            accs.append((pt[:, None, :] @ vt)[:, 0])
+        return merge_states(torch.stack(ms, 1).contiguous(), torch.stack(ls, 1).contiguous(),
+                            torch.stack(accs, 1).contiguous(), self.dtype)
+
+    @torch.no_grad()
+    def step(self, token: torch.Tensor, tau_mode) -> torch.Tensor:
+        """One decode step for a (1,) token; returns logits (1, vocab)."""
+        s = self.s
+        pos = torch.full((1,), self.length, device=self.dev, dtype=torch.long)
+        x = self.embed[token]
+        for i, L in enumerate(self.layers):
+            q, k, v = self._qkv(L, _rms(x, L["ln1"], s.eps), pos)
+            self.k_cache[i][:, self.length] = k[:, 0]
+            self.v_cache[i][:, self.length] = v[:, 0]
+            self.length += 1
+            a = self._attend(i, q[:, 0].contiguous(), tau_mode)
+            self.length -= 1
+            x = x + a.reshape(1, -1) @ L["wo"]
+            x = self._mlp(L, x)
+        self.length += 1
+        return _rms(x, self.norm, s.eps) @ self.lm_head
+
+    @torch.no_grad()
+    def generate(self, prompt: torch.Tensor, steps: int, tau_mode="median") -> Dict:
+        """Greedy decoding: prefill, then ``steps`` decode steps; per-step device time."""
+        self.length = 0
+        self.tau = [None] * self.s.layers
+        logits = self.prefill(prompt)
+        tok = logits.argmax(-1)
+        out, times = [int(tok)], []
+        for _ in range(steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            logits = self.step(tok, tau_mode)
+            tok = logits.argmax(-1)
+            b.record()
+            out.append(tok)
+            times.append((a, b))
+        torch.cuda.synchronize()
+        ms = [x.elapsed_time(y) for x, y in times]
+        return {"tokens": [int(t) for t in out], "ms_per_token": sorted(ms)[len(ms) // 2],
+                "ms_mean": sum(ms) / len(ms), "tau": self.tau, "final_length": self.length}
