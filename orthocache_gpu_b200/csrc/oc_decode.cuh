@@ -720,14 +720,16 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 
   // descriptor of ring slot `lane` (lanes < NSLOT): flattened tile (-1: empty),
   // V copy flag, unit and tile index
-  int64_t dsc_f = -1;
-  int dsc_v = 0, dsc_u = 0, dsc_t = 0;
+  //   dsc_a = 2 * (f - fa) + (V copy), or -1 for an empty slot; dsc_b = (unit << 20) | tile
+  int dsc_a = -1, dsc_b = 0;
   const int u_first = (fb > fa) ? upper_index(tp, U, fa) : 0;
   int u_iss = u_first, seq_iss = 0, kvh_iss = 0;
+  int64_t u_end_iss = 0;  // first flattened tile after unit u_iss
   int64_t f_iss = fa;
   SplitIter it_iss;
   auto enter_unit = [&](int u, int64_t f) {  // issue cursor enters unit u at flattened tile f
     u_iss = u;
+    u_end_iss = tp[u + 1];
     seq_iss = unit_seq(u);
     kvh_iss = unit_kvh(u);
     if constexpr (ATTN && TC) {
@@ -742,7 +744,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     const long long i0 = clock64();
 #endif
     if (f_iss < fb) {
-      if (f_iss >= tp[u_iss + 1]) {
+      if (f_iss >= u_end_iss) {
         int u = u_iss + 1;
         while (f_iss >= tp[u + 1]) ++u;
         enter_unit(u, f_iss);
@@ -750,15 +752,13 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       const int tile = it_iss.tile();
       issue(s, seq_iss, kvh_iss, tile, false);
       if (lane == (int)s) {
-        dsc_f = f_iss;
-        dsc_v = 0;
-        dsc_u = u_iss;
-        dsc_t = tile;
+        dsc_a = 2 * (int)(f_iss - fa);
+        dsc_b = (u_iss << 20) | tile;
       }
       it_iss.next();
       ++f_iss;
     } else if (lane == (int)s) {
-      dsc_f = -1;
+      dsc_a = -1;
     }
 #ifdef OC_PROBE_WAIT
     pw_iss += clock64() - i0;
@@ -773,11 +773,12 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 
   for (uint32_t j = 0;; ++j) {
     const uint32_t s = j % NSLOT;
-    if (!__any_sync(0xffffffffu, lane < NSLOT && dsc_f >= 0)) break;
-    const int64_t f = __shfl_sync(0xffffffffu, dsc_f, s);
-    const int isv = __shfl_sync(0xffffffffu, dsc_v, s);
-    const int u = __shfl_sync(0xffffffffu, dsc_u, s);
-    const int tile = __shfl_sync(0xffffffffu, dsc_t, s);
+    if (!__any_sync(0xffffffffu, lane < NSLOT && dsc_a >= 0)) break;
+    const int da = __shfl_sync(0xffffffffu, dsc_a, s);
+    const int db = __shfl_sync(0xffffffffu, dsc_b, s);
+    const int64_t f = da < 0 ? -1 : fa + (da >> 1);
+    const int isv = da & 1;
+    const int u = db >> 20, tile = db & ((1 << 20) - 1);
     if (f < 0) {
       issue_next(s);
       continue;
@@ -1024,7 +1025,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
           }
           __syncwarp();  // K tile read, logits stored: the slot takes this tile's V
           issue(s, seq_k, kvh_k, tile, true);
-          if (lane == (int)s) dsc_v = 1;
+          if (lane == (int)s) dsc_a |= 1;
           v_issued = true;
         }
       }
@@ -1180,7 +1181,8 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       if (acc_unit >= 0) {
         const int64_t ua = tp[acc_unit], uend = tp[acc_unit + 1] < fb ? tp[acc_unit + 1] : fb;
         if (f_gated >= uend &&
-            !__any_sync(0xffffffffu, lane < NSLOT && dsc_f >= ua && dsc_f < uend && dsc_v != 0)) {
+            !__any_sync(0xffffffffu, lane < NSLOT && dsc_a >= 0 && (dsc_a & 1) && fa + (dsc_a >> 1) >= ua &&
+                                         fa + (dsc_a >> 1) < uend)) {
 #ifdef OC_PROBE_WAIT
           const long long f0 = clock64();
 #endif
