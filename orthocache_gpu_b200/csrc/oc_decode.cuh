@@ -770,6 +770,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   int seq_k = 0, kvh_k = 0, chunk_k = 0;
   int64_t f_gated = fa;              // K tiles [fa, f_gated) are gated
   int acc_unit = -1;                 // unit held by the accumulator
+  int64_t uend_k = 0, ua_acc = 0, uend_acc = 0;  // range of the K unit / accumulator unit in [fa, fb)
 
   for (uint32_t j = 0;; ++j) {
     const uint32_t s = j % NSLOT;
@@ -792,6 +793,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       // ================================================ K tile: gate (+ logits)
       if (u != u_k) {
         u_k = u;
+        uend_k = tp[u + 1] < fb ? tp[u + 1] : fb;
         kept_k = 0;
         seq_k = unit_seq(u);
         kvh_k = unit_kvh(u);
@@ -1034,7 +1036,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         issue_next(s);
       }
       if constexpr (ATTN) {
-        const int64_t uend = tp[u + 1] < fb ? tp[u + 1] : fb;
+        const int64_t uend = uend_k;
 #ifdef OC_PROBE_WAIT
         const long long f0 = clock64();
 #endif
@@ -1045,7 +1047,11 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       }
     } else {
       // ================================================ V tile of a retained tile
-      acc_unit = u;
+      if (acc_unit != u) {
+        acc_unit = u;
+        ua_acc = tp[u];
+        uend_acc = tp[u + 1] < fb ? tp[u + 1] : fb;
+      }
       if constexpr (TC) {
         // B = P (tokens x 8 columns).  Up to 4 queries: column n carries the
         // 16-bit head (n < 4) or tail (n >= 4) of query n & 3, so one MMA adds
@@ -1179,7 +1185,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 #endif
     if constexpr (ATTN) {
       if (acc_unit >= 0) {
-        const int64_t ua = tp[acc_unit], uend = tp[acc_unit + 1] < fb ? tp[acc_unit + 1] : fb;
+        const int64_t ua = ua_acc, uend = uend_acc;
         if (f_gated >= uend &&
             !__any_sync(0xffffffffu, lane < NSLOT && dsc_a >= 0 && (dsc_a & 1) && fa + (dsc_a >> 1) >= ua &&
                                          fa + (dsc_a >> 1) < uend)) {
