@@ -298,7 +298,8 @@ struct Cfg {
   static constexpr int OFF_LGS = NW * NSLOT * SLOT;         // logits of slot s: [NW][NSLOT][GC*64] floats
   static constexpr int OFF_BAR = OFF_LGS + NW * NSLOT * LGB;  // full barrier of each slot
   static constexpr int OFF_XCH = OFF_BAR + 8 * NW * NSLOT;    // band energies exchanged in a team: [NW/P][2][P] float2
-  static constexpr int OFF_TP = OFF_XCH + 16 * NW;
+  static constexpr int OFF_STG = OFF_XCH + 16 * NW;              // finalize staging, 64 floats a warp (8-byte aligned)
+  static constexpr int OFF_TP = OFF_STG + 256 * NW;
   static constexpr int OFF_MISC = OFF_TP + 4 * (MAXU + 1);
   static constexpr int SMEM = (OFF_MISC + 4 * 32 + 127) / 128 * 128 + 1024;  // + base alignment slack
   static_assert(C >= 1 && C <= 32 && (C & (C - 1)) == 0, "K row bytes must be a power of two in 16..512");
@@ -381,6 +382,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   float* lgs_all = reinterpret_cast<float*>(smem + CF::OFF_LGS);  // [NW][NSLOT][GC*64]
   float* lgs_base = lgs_all + warp * NSLOT * (CF::LGB / 4);
   float2* xch = reinterpret_cast<float2*>(smem + CF::OFF_XCH) + team * 2 * P;
+  float* stg = reinterpret_cast<float*>(smem + CF::OFF_STG) + warp * 64;  // finalize staging
   const uint32_t bar0 = smem_u32(smem + CF::OFF_BAR) + 8u * warp * NSLOT;  // this warp's slot barriers
   if (lane < NSLOT) mbar_init(bar0 + 8u * lane, 1);
   mbar_init_fence();
@@ -649,17 +651,27 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         }
         float lq = l_mine + __shfl_xor_sync(0xffffffffu, l_mine, 1);
         lq += __shfl_xor_sync(0xffffffffu, lq, 2);
-        const int qa = 2 * t4, qb = 2 * t4 + 1;
-        const float ma = __shfl_sync(0xffffffffu, m_mine, (8 * t4) & 31);
-        const float mb = __shfl_sync(0xffffffffu, m_mine, (8 * t4 + 4) & 31);
-        const float la = __shfl_sync(0xffffffffu, lq, (8 * t4) & 31);
-        const float lb = __shfl_sync(0xffffffffu, lq, (8 * t4 + 4) & 31);
+        // one query at a time: the lanes holding its columns stage them in
+        // shared memory, then every lane writes two consecutive columns
+        static_assert(!TC || HDL == 64, "tensor-core panels are 64 columns");
+        const float2* stg2 = reinterpret_cast<const float2*>(stg);
 #pragma unroll
-        for (int mt = 0; mt < HDL / 16; ++mt) {
-          put(qa, 16 * mt + g8, ma, la, tacc[mt][0]);
-          put(qb, 16 * mt + g8, mb, lb, tacc[mt][1]);
-          put(qa, 16 * mt + g8 + 8, ma, la, tacc[mt][2]);
-          put(qb, 16 * mt + g8 + 8, mb, lb, tacc[mt][3]);
+        for (int q = 0; q < GC; ++q) {
+          if (!empty) {
+            if (t4 == (q >> 1)) {
+#pragma unroll
+              for (int mt = 0; mt < HDL / 16; ++mt) {
+                stg[16 * mt + g8] = tacc[mt][q & 1];
+                stg[16 * mt + g8 + 8] = tacc[mt][2 + (q & 1)];
+              }
+            }
+            __syncwarp();
+          }
+          const float2 v = empty ? make_float2(0.f, 0.f) : stg2[lane];
+          const float mq = __shfl_sync(0xffffffffu, m_mine, 4 * q), lqq = __shfl_sync(0xffffffffu, lq, 4 * q);
+          put(q, 2 * lane, mq, lqq, v.x);
+          put(q, 2 * lane + 1, mq, lqq, v.y);
+          __syncwarp();
         }
         if (!direct && t4 == 0 && g8 < GC)
           *reinterpret_cast<float2*>(rec_of(slot, g8) + HDL) =
