@@ -7,23 +7,24 @@
 //   * paged KV (block-table gather) ............ paged_eviction.py:56-237
 //   * mask / zeta scoring only ................. fwht_fused_prototype.py:102-192
 //
-// Design: one persistent CTA per SM, every warp an independent decoder with
-// its own shared-memory ring of tile slots (16-byte cp.async copies, one
-// commit group per slot, consumed in order), so the per-tile path has no
-// CTA-wide or grid-wide barrier.
+// Design: one persistent CTA per SM.  On the tensor-core path a team of
+// HD/64 warps shares each tile (one 64-column panel per warp); otherwise a
+// team is one warp.  Every warp has its own shared-memory ring of tile slots
+// filled by TMA (one mbarrier per slot, consumed in order), so the per-tile
+// path has no CTA-wide or grid-wide barrier; a team's warps meet only at a
+// named barrier to add their panels' band energies and logits.
 //
 //   The tiles of all units (sequence, kv head, query chunk) are flattened
-//   (oc_plan.h) and split into equal contiguous ranges, one per warp; inside a
+//   (oc_plan.h) and split into equal contiguous ranges, one per team; inside a
 //   unit the order is the reference's interleaved split order, so a range
-//   samples the whole sequence and retained work evens out across warps.  A
-//   warp scores each 64-token K tile; for a retained tile it computes the
-//   query logits (fp32, log2 domain) into the slot's logit area and reuses the
-//   slot for the tile's V, which is consumed after the copies already in
-//   flight.  An evicted tile costs one K read; its V is never read.  A unit's
-//   online-softmax state is written once its K tiles in the range are gated
-//   and no V copy of it is pending: directly when the range holds the whole
-//   unit, else as a partial state that the last of the unit's warps merges
-//   (log-sum-exp, atomic ticket), so one launch gives the final output.
+//   samples the whole sequence.  A team scores each 64-token K tile; for a
+//   retained tile it computes the query logits (fp32, log2 domain) into the
+//   slot's logit area and reuses the slot for the tile's V, which is consumed
+//   after the copies already in flight.  An evicted tile costs one K read;
+//   its V is never read.  A unit's online-softmax state is written once its K
+//   tiles in the range are gated and no V copy of it is pending: directly
+//   when the range holds the whole unit, else as a partial state that
+//   merge_kernel (a programmatic dependent launch) combines by log-sum-exp.
 //
 // Band energies use closed forms of the natural-order 64-point Walsh
 // transform along the token axis of the tile (no 64x64 matmul):
@@ -45,7 +46,6 @@
 #pragma once
 
 #include <cuda.h>
-#include <cstdio>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
@@ -82,10 +82,6 @@ constexpr int kUnrollPairs = OC_UNROLL_PAIRS;
 #define OC_MAX_WARPS_PER_CTA 8
 #endif
 constexpr int kMaxWarpsPerCta = OC_MAX_WARPS_PER_CTA;
-#ifndef OC_COPY_SPLIT
-#define OC_COPY_SPLIT 1
-#endif
-constexpr int kCopySplit = OC_COPY_SPLIT;
 constexpr int kUnrollPV = OC_UNROLL_PV;
 
 struct DecodeParams {
@@ -475,25 +471,10 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 
   // Wait for the copy in slot s (bounded; a timeout sets the status bit).
   uint32_t phases = 0;  // bit s: parity of slot s's next completion
-#ifdef OC_PROBE_WAIT
-  long long pw_wait = 0, pw_t0 = clock64(), pw_gate = 0, pw_iss = 0, pw_first = 0, pw_fin = 0, pw_fa = 0, pw_fm = 0, pw_kc = 0, pw_vc = 0;
-  int pw_kn = 0, pw_vn = 0;
-  unsigned long long pw_g0;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(pw_g0));
-  int pw_n = 0;
-#endif
   auto wait_slot = [&](uint32_t s) {
-#ifdef OC_PROBE_WAIT
-    const long long a0 = clock64();
-#endif
     if (!mbar_wait_bounded(bar0 + 8u * s, (phases >> s) & 1u, kWaitLimit) && lane == 0)
       atomicOr(p.status, ST_TIMEOUT);
     phases ^= 1u << s;
-#ifdef OC_PROBE_WAIT
-    pw_wait += clock64() - a0;
-    if (pw_n == 0) pw_first = clock64() - pw_t0;
-    ++pw_n;
-#endif
     __syncwarp();
     return ring + s * SLOT;
   };
@@ -568,15 +549,13 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   };
 
 
-  // ======================================================== phase A: K stream
   // ======================================================== single pass
-  // Warp wg owns the flattened K tiles [fa, fb) (unit-major, split-major inside
+  // Team wg owns the flattened K tiles [fa, fb) (unit-major, split-major inside
   // a unit, so a range interleaves over the sequence).  It gates each tile and
   // streams the V of a retained tile into the ring slot its K tile just left;
-  // the ring is one FIFO of copies (one cp.async group per slot).  A unit's
-  // state is written once all its K tiles in the range are gated and no V copy
-  // of it is pending: directly when the range holds the whole unit, else as a
-  // partial state merged by the last of the unit's warps.
+  // the ring is one FIFO of copies.  A unit's state is written once all its K
+  // tiles in the range are gated and no V copy of it is pending: directly when
+  // the range holds the whole unit, else as a partial state for merge_kernel.
   const int64_t WE = (N < W) ? (N > 0 ? N : 1) : W;  // warps with a tile range
   const bool active = wg < WE;
   const int64_t fa = active ? range_lo(wg, N, WE) : 0, fb = active ? range_lo(wg + 1, N, WE) : 0;
@@ -752,9 +731,6 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   };
   if (fb > fa) enter_unit(u_first, fa);
   auto issue_next = [&](uint32_t s) {
-#ifdef OC_PROBE_WAIT
-    const long long i0 = clock64();
-#endif
     if (f_iss < fb) {
       if (f_iss >= u_end_iss) {
         int u = u_iss + 1;
@@ -772,9 +748,6 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     } else if (lane == (int)s) {
       dsc_a = -1;
     }
-#ifdef OC_PROBE_WAIT
-    pw_iss += clock64() - i0;
-#endif
   };
   for (uint32_t s = 0; s < NSLOT; ++s) issue_next(s);
 
@@ -797,9 +770,6 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       continue;
     }
     unsigned char* ts = wait_slot(s);
-#ifdef OC_PROBE_WAIT
-    const long long it0 = clock64();
-#endif
     float* lgs = lgs_base + s * (CF::LGB / 4);
     if (!isv) {
       // ================================================ K tile: gate (+ logits)
@@ -883,13 +853,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       // ---- band energies
       float score;
       if constexpr (TC) {
-#ifdef OC_PROBE_WAIT
-        const long long g0 = clock64();
         score = tc_gate(ts);
-        pw_gate += clock64() - g0;
-#else
-        score = tc_gate(ts);
-#endif
       } else {
         float2 sres[NRES][D2];
         float2 ehd[D2];  // one E_high accumulator per column pair: independent FMA chains
@@ -1049,13 +1013,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       }
       if constexpr (ATTN) {
         const int64_t uend = uend_k;
-#ifdef OC_PROBE_WAIT
-        const long long f0 = clock64();
-#endif
         if (f + 1 == uend && kept_k == 0) finalize(u, true);
-#ifdef OC_PROBE_WAIT
-        pw_fin += clock64() - f0;
-#endif
       }
     } else {
       // ================================================ V tile of a retained tile
@@ -1192,22 +1150,13 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       __syncwarp();
       issue_next(s);
     }
-#ifdef OC_PROBE_WAIT
-    if (isv) { pw_vc += clock64() - it0; ++pw_vn; } else { pw_kc += clock64() - it0; ++pw_kn; }
-#endif
     if constexpr (ATTN) {
       if (acc_unit >= 0) {
         const int64_t ua = ua_acc, uend = uend_acc;
         if (f_gated >= uend &&
             !__any_sync(0xffffffffu, lane < NSLOT && dsc_a >= 0 && (dsc_a & 1) && fa + (dsc_a >> 1) >= ua &&
                                          fa + (dsc_a >> 1) < uend)) {
-#ifdef OC_PROBE_WAIT
-          const long long f0 = clock64();
-#endif
           finalize(acc_unit, false);
-#ifdef OC_PROBE_WAIT
-          pw_fin += clock64() - f0;
-#endif
           acc_unit = -1;
           reset_state();
         }
@@ -1218,14 +1167,6 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // this CTA's decode work is issued: the merge grid may be scheduled (its
   // griddepcontrol.wait still waits for the whole grid to complete)
   if constexpr (ATTN) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-#ifdef OC_PROBE_WAIT
-  unsigned long long pw_g1;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(pw_g1));
-  if (lane == 0 && warp == 0)
-    printf("PW blk %d w %d items %d total %lld first %lld fin %lld K %lld x%d V %lld x%d cyc/item %lld wait %lld gate %lld issue %lld g0 %llu ns %llu\n",
-           blockIdx.x, warp, pw_n, clock64() - pw_t0, pw_first, pw_fin, pw_kc / (pw_kn ? pw_kn : 1), pw_kn, pw_vc / (pw_vn ? pw_vn : 1), pw_vn, (clock64() - pw_t0) / (pw_n ? pw_n : 1),
-           pw_wait / (pw_n ? pw_n : 1), pw_gate / (pw_n ? pw_n : 1), pw_iss / (pw_n ? pw_n : 1), pw_g0 % 1000000000ull, pw_g1 - pw_g0);
-#endif
 }
 
 // Merge of the units that several teams share, launched as a programmatic

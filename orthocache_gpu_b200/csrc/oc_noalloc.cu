@@ -8,9 +8,9 @@
 // process exits.  In host code `g_scratch` only names the array: its device
 // address comes from cudaGetSymbolAddress, looked up once per device on the
 // first call with that device current (so make the first call before any
-// stream capture).  All calls share the array; the merge tickets at its start
-// are zeroed on the stream before every launch, so a failed launch cannot
-// poison the next one, but calls that overlap on the GPU race.
+// stream capture).  All calls share the array; its header is zeroed on the
+// stream before every launch, so a failed launch cannot poison the next one,
+// but calls that overlap on the GPU race.
 #include <mutex>
 
 #include "../../include/orthocache_b200.h"

@@ -1,16 +1,14 @@
-// Work decomposition of the two-phase decode kernel.  Plain integer
-// arithmetic shared by device code and host-side checks.
+// Work decomposition of the decode kernel.  Plain integer arithmetic shared
+// by device code and host-side checks.
 //
 // Units: u = (seq * num_kv_heads + kv_head) * chunks + chunk, each with T_u
 // tiles.  Tiles of all units are flattened unit-major; inside a unit the order
 // is split-major with the reference's interleaved assignment (split s owns
 // tiles s, s+S, s+2S, ... ; fused_eviction.py:259).
 //
-// Phase A: warp w of W gates flattened tiles [range_lo(w, N, W), range_lo(w+1, N, W)).
-// Phase B: the Kt retained tiles, ranked in flattened order, are split over
-// WB = min(W, Kt) warps the same way (so no warp range is empty); a unit's
-// retained ranks [R0, R1] are covered by warps owner(R0) .. owner(R1).  A
-// warp stores at most two partial states: slot 2w for the first unit of its
+// Team w of W gates flattened tiles [range_lo(w, N, W), range_lo(w+1, N, W));
+// a unit's tiles [R0, R1] are covered by teams owner(R0) .. owner(R1).  A
+// team stores at most two partial states: slot 2w for the first unit of its
 // range, 2w+1 for its last unit when that differs and is shared.
 #pragma once
 

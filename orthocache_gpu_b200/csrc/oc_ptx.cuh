@@ -1,5 +1,5 @@
-// Inline-PTX helpers for the sm_100a decode kernels: mbarriers and the
-// bulk-async (TMA engine) global->shared copy.  No cluster multicast is used
+// Inline-PTX helpers for the sm_100a decode kernels: mbarriers, the
+// tiled TMA load, ldmatrix and mma.sync.  No cluster multicast is used
 // anywhere in this library: every copy lands in the issuing CTA's own shared
 // memory, and sources are always this GPU's memory.
 #pragma once
@@ -56,55 +56,6 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return pol;
 }
 
-// Bulk async copy global -> this CTA's shared memory, completing `bytes`
-// transactions on mbarrier `bar`.  dst, src and bytes must be multiples of 16.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
-                                         uint32_t bar, uint64_t pol) {
-#ifdef OC_PROBE_NO_HINT
-  (void)pol;
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
-  return;
-#endif
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
-      : "memory");
-}
-
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr));
-  return v;
-}
-
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
-}
-
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-
-// 16-byte asynchronous global -> shared copy (LDGSTS), L2 evict-first, no L1.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t pol) {
-  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(pol)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // ldmatrix: four 8x8 b16 matrices; lanes 8i..8i+7 give the row addresses of matrix i.
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -145,12 +96,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int 
       " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
       "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(pol)
       : "memory");
-}
-
-// Order this thread's earlier generic-proxy shared-memory accesses before
-// later async-proxy (TMA) writes to the same addresses.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 }  // namespace oc
