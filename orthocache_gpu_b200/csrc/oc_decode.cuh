@@ -69,6 +69,10 @@ enum : int { LAYOUT_LINEAR = 0, LAYOUT_PAGED = 1 };
 enum : uint32_t { ST_TIMEOUT = 1u, ST_BAD_PAGE = 2u, ST_BAD_SEQLEN = 4u };
 
 constexpr uint32_t kWaitLimit = 1u << 22;
+#ifndef OC_TILES_PER_TEAM
+#define OC_TILES_PER_TEAM 1
+#endif
+constexpr int kTilesPerTeam = OC_TILES_PER_TEAM;  // grid sizing for small problems
 
 // Unroll factors of the per-tile row loops (instruction-cache footprint).
 #ifndef OC_UNROLL_PAIRS
@@ -1273,9 +1277,9 @@ cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tk, const CU
   }
   const int nchunks = (p.group + GC - 1) / GC;
   const int64_t tiles = (int64_t)p.num_seqs * p.num_kv_heads * nchunks * p.num_tiles;
-  // about two tiles per team, at most one wave of resident CTAs
+  // about kTilesPerTeam tiles per team, at most one wave of resident CTAs
   constexpr int kTeams = CF::NW / CF::P;
-  const int64_t want = (tiles + 2 * kTeams - 1) / (2 * kTeams);
+  const int64_t want = (tiles + kTilesPerTeam * kTeams - 1) / (kTilesPerTeam * kTeams);
   // at most one wave of resident CTAs on this device, whatever num_sms says
   static int dev_sms[64] = {0};
   if (dev_sms[dev] == 0) cudaDeviceGetAttribute(&dev_sms[dev], cudaDevAttrMultiProcessorCount, dev);
