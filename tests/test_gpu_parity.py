@@ -190,7 +190,7 @@ def test_v1_single_tile_and_empty_sequence():
 
 
 # ------------------------------------------------------------ V3
-@pytest.mark.parametrize("group", [1, 2, 4, 8, 3])
+@pytest.mark.parametrize("group", [1, 2, 4, 8, 3, 16])  # 16: two query chunks per kv head
 def test_v3_groups(group):
     from orthocache_gpu_b200.synthetic import gqa_inputs
     x = gqa_inputs(2, group, 1024, 128, seed=group)
@@ -242,3 +242,36 @@ def test_paged_mha_zeta_equals_v2_per_sequence():
     ref, _ = orc.paged_attention(cast_np(x.q, dt), cast_np(x.k_cache, dt), cast_np(x.v_cache, dt),
                                  x.block_tables, zeta_max=1.0)
     assert_close(out, ref, dt, "paged mha zeta")
+
+
+def test_v3_more_units_than_one_launch():
+    # 300 sequences x 8 kv heads = 2400 units: the library splits the batch
+    # into launches of at most 2048 units that share one workspace
+    from orthocache_gpu_b200.synthetic import gqa_inputs
+    x = gqa_inputs(8, 1, 128, 64, seed=5, batch=300)
+    dt = torch.float16  # two tiles a sequence: outputs near 1, where bf16 rounding alone exceeds 2e-3
+    q, k, v = (cast_np(a, dt) for a in (x.q, x.keys, x.values))
+    out, meta = oc.fused_orthocache_attention_v3_gqa(T(x.q, dt), T(x.keys, dt), T(x.values, dt), 100.0, 1)
+    assert out.shape == (300, 8, 64)
+    kept = 0
+    for b in range(300):
+        ref, rm = orc.v3_gqa_attention(q[b], k[b], v[b], 100.0, 1)
+        kept += rm["tiles_retained"]
+        assert_close(out[b], ref, dt, f"v3 batch element {b}")
+    assert meta["tiles_retained"] == kept
+
+
+def test_paged_batch_with_an_empty_sequence():
+    from orthocache_gpu_b200.synthetic import paged_inputs
+    x = paged_inputs(4, 2, 4, 128, 32, 256, 1024, seed=9)
+    lens = x.seq_lens.copy()
+    lens[1] = 0
+    dt = torch.float16
+    q, kc, vc, bt, _ = x.torch(dt, DEV)
+    sl = torch.from_numpy(lens).to(DEV)
+    ref, keep = orc.paged_attention(cast_np(x.q, dt), cast_np(x.k_cache, dt), cast_np(x.v_cache, dt),
+                                    x.block_tables, tau=150.0, seq_lens=lens)
+    out, meta = oc.fused_orthocache_attention_paged(q, kc, vc, bt, None, seq_lens=sl, tau=150.0)
+    assert meta["tiles_retained"] == int(keep.sum())
+    assert out[1].abs().max().item() == 0.0
+    assert_close(out, ref, dt, "paged with an empty sequence")
