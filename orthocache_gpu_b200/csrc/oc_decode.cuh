@@ -369,12 +369,8 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   const int team = warp / P, panel = warp % P;
   const int64_t W = (int64_t)gridDim.x * (NW / P);        // teams in the grid
   const int64_t wg = (int64_t)blockIdx.x * (NW / P) + team;  // this warp's team
-  uint32_t nsync = 0;  // team barriers passed (the same count in every warp of the team)
   auto team_sync = [&]() {
-    if constexpr (P > 1) {
-      asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "r"(32 * P) : "memory");
-      ++nsync;
-    }
+    if constexpr (P > 1) asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "r"(32 * P) : "memory");
   };
   const int nchunks = (p.group + GC - 1) / GC;
   const int U = p.num_seqs * p.num_kv_heads * nchunks;
@@ -721,7 +717,6 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // V copy flag, unit and tile index
   //   dsc_a = 2 * (f - fa) + (V copy), or -1 for an empty slot; dsc_b = (unit << 20) | tile
   int dsc_a = -1, dsc_b = 0;
-  uint32_t dsc_sync = 0;  // team barriers passed when a retained tile's logits were stored
   const int u_first = (fb > fa) ? upper_index(tp, U, fa) : 0;
   int u_iss = u_first, seq_iss = 0, kvh_iss = 0;
   int64_t u_end_iss = 0;  // first flattened tile after unit u_iss
@@ -771,7 +766,6 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     if (!__any_sync(0xffffffffu, lane < NSLOT && dsc_a >= 0)) break;
     const int da = __shfl_sync(0xffffffffu, dsc_a, s);
     const int db = __shfl_sync(0xffffffffu, dsc_b, s);
-    const uint32_t logits_sync = __shfl_sync(0xffffffffu, dsc_sync, s);
     const int64_t f = da < 0 ? -1 : fa + (da >> 1);
     const int isv = da & 1;
     const int u = db >> 20, tile = db & ((1 << 20) - 1);
@@ -1013,10 +1007,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
           }
           __syncwarp();  // K tile read, logits stored: the slot takes this tile's V
           issue(s, seq_k, kvh_k, tile, true);
-          if (lane == (int)s) {
-            dsc_a |= 1;
-            dsc_sync = nsync;
-          }
+          if (lane == (int)s) dsc_a |= 1;
           v_issued = true;
         }
       }
@@ -1043,10 +1034,8 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         constexpr bool PACK = GC <= 4;
         const int qg = PACK ? (g8 & 3) : g8;
         const bool qok = qg < GC;
-        // logits: the sum of the team's panel partials, in panel order; the
-        // teammates' partials are visible once a team barrier has followed
-        // their stores (every non-empty item has one), so wait only if none has
-        if (nsync == logits_sync) team_sync();
+        // logits: the sum of the team's panel partials, in panel order
+        team_sync();
         auto lg2 = [&](int o) -> float2 {
           if constexpr (P == 1) {
             return *reinterpret_cast<const float2*>(lgs + o);
