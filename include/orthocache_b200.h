@@ -27,12 +27,12 @@
  * Thresholds are given in double precision and compared exactly as the
  * reference's CPU path compares them (see the notes at each function).
  *
- * Workspace: a fixed header (merge tickets) followed by the split partial
- * states; its size depends only on the query group and head_dim.  Size it with oc_workspace_bytes(); it must be
- * zero-filled once before first use and every launch leaves the header zeroed
- * again.  Launches that share a workspace must not overlap on the GPU.  A
- * non-zero *status word after a launch (OC_STATUS_*) means the outputs of that
- * launch are invalid; re-zero the workspace before reusing it.
+ * Workspace: a fixed header (the per-unit tile prefix, written by every
+ * launch for the merge kernel) followed by the split partial states; its size
+ * depends only on the query group and head_dim.  Size it with
+ * oc_workspace_bytes(); it needs no initialisation.  Launches that share a
+ * workspace must not overlap on the GPU.  A non-zero *status word after a
+ * launch (OC_STATUS_*) means the outputs of that launch are invalid.
  */
 #ifndef ORTHOCACHE_B200_H
 #define ORTHOCACHE_B200_H
@@ -175,8 +175,8 @@ int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_strid
  * exceed 2 MiB (head_dim 256) returns OC_ERR_TOO_LARGE.  It calls no cudaMalloc or
  * cudaFree.  The first call on each device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture.  Every call zeroes the array's merge
- * tickets on the stream, and all calls share the one array: calls that
+ * call before any stream capture.  Every call zeroes the array's header on
+ * the stream, and all calls share the one array: calls that
  * overlap on the GPU (different streams, or different host threads) race
  * and give wrong results. */
 int oc_fused_attention_v2_noalloc(const void* q, int q_dtype, int64_t q_head_stride,
