@@ -1,6 +1,6 @@
 """Benchmark of the fused spectral-eviction decode kernel (B200).
 
-Workload (BASELINE config 2 at its headline size): V2 multi-head decode,
+Workload (the headline configuration): V2 multi-head decode,
 32 heads, head_dim 128, 32K tokens, fp16, the 50/50 smooth/noisy tile
 mixture, ζ_max = 1.0 (≈50 % eviction).  One step = one decode call over one
 batch of synthetic input.  ``value`` = algorithmic bytes (all K read once +
@@ -18,6 +18,7 @@ the timed region is the max over ranks.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -302,7 +303,8 @@ def cpu_baseline(seq, sample_heads=8, min_seconds=10.0):
         cores = len(os.sched_getaffinity(0))
     except AttributeError:
         cores = os.cpu_count()
-    return {"value": nb / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+    return {"value": nb / dt / 1e9, "unit": "GB/s", "cores": cores, "torch_threads": torch.get_num_threads(),
+            "kind": "port",
             "sample": f"{sample_heads} of {HEADS} heads x {seq} tokens (same mixture), oracle NumPy "
                       f"float32/64, {reps} passes in {dt:.1f} s"}
 
@@ -317,7 +319,8 @@ def main():
         return
     if dist:
         torch.cuda.set_device(local)
-        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local))
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                             timeout=datetime.timedelta(seconds=120))
     dev = torch.device("cuda", local)
     seq = a.seq
     ntiles = HEADS * (seq // 64)

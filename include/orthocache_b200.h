@@ -31,8 +31,12 @@
  * launch for the merge kernel) followed by the split partial states; its size
  * depends only on the query group and head_dim.  Size it with
  * oc_workspace_bytes(); it needs no initialisation.  Launches that share a
- * workspace must not overlap on the GPU.  A non-zero *status word after a
- * launch (OC_STATUS_*) means the outputs of that launch are invalid.
+ * workspace must not overlap on the GPU.
+ *
+ * Status word: launches OR error bits (OC_STATUS_*) into *status and never
+ * clear it, so a non-zero word means that some launch since the caller last
+ * cleared it produced invalid outputs.  Callers that check after every call
+ * clear it after reading; callers that batch launches check it once.
  */
 #ifndef ORTHOCACHE_B200_H
 #define ORTHOCACHE_B200_H
@@ -87,7 +91,9 @@ int oc_fwht_eviction(const void* keys, int k_dtype, int64_t num_tokens, int head
  * (num_heads, head_dim) with out_head_stride.  A tile is evicted iff
  * ζ > zeta_max in double precision (fused_eviction.py:428-432), so a NaN ζ
  * is retained.  mask_out (nullable): (num_heads, seq_len/64) retain flags.
- * retained (nullable): += number of retained tiles.  num_splits <= 0 selects
+ * retained (nullable): set to the number of retained tiles of the call
+ * (written on the stream by the launch itself; no zeroing needed).
+ * num_splits <= 0 selects
  * oc_auto_num_splits(num_tiles, num_sms). */
 int oc_fused_attention_v2(const void* q, int q_dtype, int64_t q_head_stride,
                           const void* keys, int k_dtype, int64_t k_head_stride, int64_t k_tok_stride,
@@ -129,14 +135,19 @@ int oc_fused_attention_v3_gqa(const void* q, int q_dtype, int64_t q_seq_stride, 
  * reference's behaviour.  gate = OC_GATE_ZETA (threshold = zeta_max, the
  * reference's paged path) or OC_GATE_CAUCHY_SCHWARZ (threshold = tau).
  * block_size: power of two.  group = 1 with OC_GATE_ZETA is exactly the
- * reference's MHA paged kernel. */
+ * reference's MHA paged kernel.  k_scale applies to float8 key caches only
+ * (other dtypes: pass 1.0 and fold any scale into q): every key element is
+ * de-quantised into q's dtype as round(float(k) * float(k_scale)) before the
+ * gate and the logits, which is the reference's k_cache.to(q.dtype) * k_scale
+ * (paged_eviction.py:355-357). */
 int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
                              const void* k_cache, int k_dtype, int64_t k_blk_stride, int64_t k_head_stride,
                              int64_t k_tok_stride, const void* v_cache, int v_dtype, int64_t v_blk_stride,
                              int64_t v_head_stride, int64_t v_tok_stride, int num_blocks, int block_size,
                              const int32_t* block_tables, int64_t bt_seq_stride, int max_blocks,
                              const int32_t* seq_lens, int num_seqs, int num_kv_heads, int group,
-                             int head_dim, int gate, double threshold, int num_splits, int num_sms,
+                             int head_dim, int gate, double threshold, double k_scale, int num_splits,
+                             int num_sms,
                              void* out, int out_dtype, int64_t out_seq_stride, int64_t out_head_stride,
                              uint8_t* mask_out, uint32_t* retained, uint32_t* status, void* workspace,
                              size_t workspace_bytes, void* stream);
@@ -175,10 +186,10 @@ int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_strid
  * exceed 2 MiB (head_dim 256) returns OC_ERR_TOO_LARGE.  It calls no cudaMalloc or
  * cudaFree.  The first call on each device looks up the array's device
  * address (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture.  Every call zeroes the array's header on
- * the stream, and all calls share the one array: calls that
- * overlap on the GPU (different streams, or different host threads) race
- * and give wrong results. */
+ * call before any stream capture.  Every launch writes the parts of the
+ * array it later reads, so nothing needs clearing between calls; all calls
+ * share the one array: calls that overlap on the GPU (different streams, or
+ * different host threads) race and give wrong results. */
 int oc_fused_attention_v2_noalloc(const void* q, int q_dtype, int64_t q_head_stride,
                                   const void* keys, int k_dtype, int64_t k_head_stride, int64_t k_tok_stride,
                                   const void* values, int v_dtype, int64_t v_head_stride, int64_t v_tok_stride,

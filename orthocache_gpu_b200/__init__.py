@@ -8,6 +8,7 @@ package needs no GPU; every compute call needs CUDA tensors and the built
 library and raises otherwise (there is no CPU fallback).
 """
 
+from ._lib import check_status
 from .fused_eviction import fused_orthocache_attention, fused_orthocache_attention_v2
 from .fwht_fused_prototype import (
     BAND_DC_64,
@@ -36,6 +37,7 @@ __all__ = [
     "BypassFlag",
     "GPUProfile",
     "format_bypass_reason",
+    "check_status",
     "TILE_SIZE",
     "BAND_DC_64",
     "BAND_LOW_64",

@@ -41,7 +41,7 @@ SIGNATURES = {
                                        _i, _i, _i, _i64, _i, _d, _i, _i, _vp, _i, _i64, _i64, _vp, _vp, _vp, _vp,
                                        _sz, _vp]),
     "oc_fused_attention_paged": (_i, [_vp, _i, _i64, _i64, _vp, _i, _i64, _i64, _i64, _vp, _i, _i64, _i64, _i64,
-                                      _i, _i, _vp, _i64, _i, _vp, _i, _i, _i, _i, _i, _d, _i, _i, _vp, _i, _i64,
+                                      _i, _i, _vp, _i64, _i, _vp, _i, _i, _i, _i, _i, _d, _d, _i, _i, _vp, _i, _i64,
                                       _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "oc_fused_attention_v2_noalloc": (_i, [_vp, _i, _i64, _vp, _i, _i64, _i64, _vp, _i, _i64, _i64, _i, _i64, _i,
                                            _d, _i, _i, _vp, _i, _i64, _vp, _vp, _vp, _vp]),
@@ -98,7 +98,13 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
     return dev
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> int:
+    """Handle of the current CUDA stream of ``device`` (a cudaStream_t as int)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -107,50 +113,107 @@ _sm_cache: dict = {}
 
 def num_sms(device: torch.device) -> int:
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    if idx not in _sm_cache:
-        _sm_cache[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
-    return _sm_cache[idx]
+    n = _sm_cache.get(idx)
+    if n is None:
+        n = _sm_cache[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return n
+
+
+_splits_cache: dict = {}
+
+
+def auto_num_splits(num_tiles: int, device: torch.device) -> int:
+    """The reference's split heuristic min(SMs, max(1, T/4), T) (fused_eviction.py:556-570)."""
+    key = (num_tiles, device.index)
+    s = _splits_cache.get(key)
+    if s is None:
+        s = _splits_cache[key] = load().oc_auto_num_splits(num_tiles, num_sms(device))
+    return s
+
+
+_wsbytes_cache: dict = {}
+
+
+def workspace_bytes(num_groups: int, group: int, num_tiles: int, head_dim: int) -> int:
+    """oc_workspace_bytes; the size depends only on the query group and head_dim."""
+    key = (group, head_dim)
+    b = _wsbytes_cache.get(key)
+    if b is None:
+        b = _wsbytes_cache[key] = load().oc_workspace_bytes(max(1, num_groups), group, num_tiles, head_dim)
+    return b
 
 
 class _Workspace:
-    """Zero-initialised split-K workspace and control words for one (device, stream)."""
+    """Split-K workspace and control words for one (device, stream).
+
+    The workspace needs no initialisation (every launch writes what it
+    reads).  ``ctrl[0]`` receives the retained-tile count of a call (written
+    by the launch), ``ctrl[1]`` is the sticky status word: launches OR error
+    bits into it and only :func:`read_stats` / :func:`check_status` clear it.
+    """
 
     def __init__(self, device):
         self.device = device
-        self.buf = torch.zeros(0, dtype=torch.uint8, device=device)
-        # ctrl[0]: retained-tile counter, ctrl[1]: status bits
+        self.buf = torch.empty(0, dtype=torch.uint8, device=device)
+        self.buf_ptr, self.buf_bytes = self.buf.data_ptr(), 0
         self.ctrl = torch.zeros(2, dtype=torch.int32, device=device)
+        self.retained_ptr = self.ctrl.data_ptr()
+        self.status_ptr = self.retained_ptr + 4
+        self.status = self.ctrl[1]  # device view of the status word (handed out in metadata)
 
-    def get(self, nbytes: int) -> torch.Tensor:
-        if self.buf.numel() < nbytes:
-            self.buf = torch.zeros(max(nbytes, 2 * self.buf.numel()), dtype=torch.uint8, device=self.device)
-        return self.buf
-
-    def reset(self) -> None:
-        self.buf.zero_()
-        self.ctrl.zero_()
+    def get(self, nbytes: int):
+        """(pointer, size) of a workspace of at least ``nbytes``."""
+        if self.buf_bytes < nbytes:
+            self.buf = torch.empty(max(nbytes, 2 * self.buf_bytes), dtype=torch.uint8, device=self.device)
+            self.buf_ptr, self.buf_bytes = self.buf.data_ptr(), self.buf.numel()
+        return self.buf_ptr, self.buf_bytes
 
 
 _ws: dict = {}
 
 
-def workspace(device: torch.device) -> _Workspace:
-    key = (device.index if device.index is not None else torch.cuda.current_device(),
-           torch.cuda.current_stream(device).cuda_stream)
+def workspace(device: torch.device, stream: int | None = None) -> _Workspace:
+    """The workspace of ``device`` for ``stream`` (default: its current stream)."""
+    if stream is None:
+        stream = stream_ptr(device)
+    key = (device.index, stream)
     w = _ws.get(key)
     if w is None:
         w = _ws[key] = _Workspace(device)
     return w
 
 
+def _raise_status(status: int) -> None:
+    bits = [m for b, m in STATUS_BITS.items() if status & b]
+    raise RuntimeError("orthocache_gpu_b200 kernel reported (a launch on this stream since the status was "
+                       "last checked): " + "; ".join(bits))
+
+
 def read_stats(ws: _Workspace) -> int:
-    """Synchronising read of the retained-tile counter; raises on a device status."""
+    """Synchronising read of the retained-tile count; raises (and clears) a device status."""
     retained, status = ws.ctrl.tolist()
     if status:
-        ws.reset()
-        bits = [m for b, m in STATUS_BITS.items() if status & b]
-        raise RuntimeError("orthocache_gpu_b200 kernel reported: " + "; ".join(bits))
+        ws.ctrl[1].zero_()
+        _raise_status(status)
     return int(retained)
+
+
+def check_status(device=None) -> None:
+    """Raise if a launch on ``device``'s current stream reported an error since the last check.
+
+    Calls made with ``stats=False`` do not synchronise and so cannot raise
+    themselves; their errors stay in the stream's sticky status word until
+    this function (or the next ``stats=True`` call on the stream) reads it.
+    Synchronises with the stream.  Clears the word after reading it.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    ws = workspace(dev)
+    status = int(ws.ctrl[1].item())
+    if status:
+        ws.ctrl[1].zero_()
+        _raise_status(status)
 
 
 def ptr(t) -> int:

@@ -176,12 +176,16 @@ int sms_or_device(int num_sms) {
 
 // Workspace layout (every region 256-byte aligned):
 //   fixed header (kFixedBytes): the per-unit tile prefix for the merge
-//     kernel (written by every launch; sized for 4 ints a unit)
+//     kernel and the per-team retained-tile counts (both written by every
+//     launch before they are read, so the workspace needs no initialisation)
 //   part  partial states, 2 slots per team of warps: 2*kMaxWarps*gc*(hd+16) f32
 constexpr int64_t kMaxUnits = 2048;  // units per launch (shared-memory prefix arrays)
 constexpr int64_t kMaxWarps = 1280;
 constexpr size_t pad256(size_t b) { return (b + 255) & ~size_t(255); }
 constexpr size_t kFixedBytes = pad256(4 * 4 * kMaxUnits);
+// per-team retained-tile counts live in the second half of the fixed header
+constexpr size_t kTeamKeptOffset = pad256(4 * (kMaxUnits + 1));
+static_assert(kTeamKeptOffset + 4 * kMaxWarps <= kFixedBytes, "fixed workspace header");
 
 struct WsLayout {
   size_t part, total;
@@ -200,6 +204,7 @@ int attach_workspace(DecodeParams& p, int64_t units, int hd, void* ws, size_t ws
   if (ws == nullptr || ws_bytes < L.total || !aligned16(ws)) return OC_ERR_WORKSPACE;
   char* b = static_cast<char*>(ws);
   p.tile_prefix = reinterpret_cast<int*>(b);
+  p.team_kept = reinterpret_cast<int*>(b + kTeamKeptOffset);
   p.part = reinterpret_cast<float*>(b + L.part);
   return OC_OK;
 }
@@ -208,6 +213,8 @@ DecodeParams blank() {
   DecodeParams p;
   std::memset(&p, 0, sizeof(p));
   p.layout = oc::LAYOUT_LINEAR;
+  p.k_deq_dtype = -1;
+  p.k_deq_scale = 1.f;
   p.block_shift = 0;
   p.num_seqs = 1;
   p.group = 1;
@@ -345,6 +352,7 @@ static int v3_common(DecodeParams& p, const void* q, int q_dtype, int64_t q_seq_
     }
     if (out) pc.out = static_cast<char*>(out) + s0 * out_seq_stride * osz;
     if (p.mask) pc.mask = p.mask + s0 * num_kv_heads * tiles;
+    pc.stats_add = s0 > 0 ? 1 : 0;  // the first launch sets the count, later ones add
     const int r = attach_workspace(pc, ns * units_per_seq, head_dim, workspace, workspace_bytes);
     if (r != OC_OK) return r;
     const int e = run(pc, k_dtype, v_dtype, head_dim, true, sms, static_cast<cudaStream_t>(stream));
@@ -422,7 +430,8 @@ int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, i
                              int64_t v_head_stride, int64_t v_tok_stride, int num_blocks, int block_size,
                              const int32_t* block_tables, int64_t bt_seq_stride, int max_blocks,
                              const int32_t* seq_lens, int num_seqs, int num_kv_heads, int group, int head_dim,
-                             int gate, double threshold, int num_splits, int num_sms, void* out, int out_dtype,
+                             int gate, double threshold, double k_scale, int num_splits, int num_sms, void* out,
+                             int out_dtype,
                              int64_t out_seq_stride, int64_t out_head_stride, uint8_t* mask_out,
                              uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
                              void* stream) {
@@ -441,6 +450,11 @@ int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, i
     return OC_ERR_INVALID;
   }
   p.thr = round_down_f32(threshold);
+  if (k_dtype == OC_F8E4M3) {  // de-quantised into q's dtype, as the reference's paged path does
+    if (q_dtype != OC_F32 && q_dtype != OC_F16 && q_dtype != OC_BF16) return OC_ERR_UNSUPPORTED;
+    p.k_deq_dtype = q_dtype;  // OC_F32/F16/BF16 equal oc::DT_F32/F16/BF16
+    p.k_deq_scale = static_cast<float>(k_scale);
+  }
   p.layout = oc::LAYOUT_PAGED;
   p.block_tables = block_tables;
   p.bt_seq_stride = bt_seq_stride;
@@ -460,8 +474,3 @@ int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, i
 }
 
 }  // extern "C"
-
-namespace oc {
-// Bytes at the start of a workspace that must be zero when a launch begins.
-size_t workspace_header_bytes() { return kFixedBytes; }
-}  // namespace oc

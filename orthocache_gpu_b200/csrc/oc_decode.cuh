@@ -117,16 +117,24 @@ struct DecodeParams {
   int64_t out_seq_stride, out_head_stride;
   int8_t* mask;       // (num_seqs, num_kv_heads, num_tiles), nullable
   float* score;       // same shape: zeta or Cauchy-Schwarz bound, nullable
-  uint32_t* stats;    // [0] += retained tiles, nullable
-  uint32_t* status;   // error bits, non-null
+  uint32_t* stats;    // [0] = retained tiles of the call (written by merge_kernel), nullable
+  int stats_add;      // 1: add this launch's count to stats[0] (later launches of one call)
+  uint32_t* status;   // error bits (sticky OR), non-null
   // workspace (attention only)
   int* tile_prefix;    // tiles of units [0, u): written by CTA 0 for merge_kernel (units + 1 ints)
+  int* team_kept;      // retained tiles gated by each team of the grid (one int per team)
   float* part;         // partial states [2 * teams][GC][P][HD/P + 4]: acc, m, l
   // shard mode (nullable): write the merged partial state (m, l, unnormalised
   // acc) of each query head instead of the normalised output
   float* sh_m;
   float* sh_l;
   float* sh_acc;
+  // float8 keys of the paged path are de-quantised as the reference does
+  // (paged_eviction.py:355-357: k_cache.to(q.dtype) * k_scale): every key
+  // element becomes round_to(k_deq_dtype, float(k) * k_deq_scale) before the
+  // gate and the logits.  k_deq_dtype < 0: keys are used as stored.
+  int k_deq_dtype;
+  float k_deq_scale;
 };
 
 // ---------------------------------------------------------------- conversions
@@ -217,6 +225,23 @@ __device__ __forceinline__ void emit(const DecodeParams& p, int seq, int hq, int
   } else {
     store_any(p.out, (int64_t)seq * p.out_seq_stride + (int64_t)hq * p.out_head_stride + d, p.out_dtype,
               a / fmaxf(l, 1e-9f));
+  }
+}
+
+// De-quantisation of float8 keys into the query dtype (see DecodeParams::k_deq_dtype).
+template <typename KT, int N>
+__device__ __forceinline__ void k_dequant(const DecodeParams& p, float2 (&f)[N]) {
+  if constexpr (std::is_same<KT, __nv_fp8_e4m3>::value) {
+    if (p.k_deq_dtype >= 0) {
+      const float s = p.k_deq_scale;
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        float2 x = make_float2(f[i].x * s, f[i].y * s);
+        if (p.k_deq_dtype == DT_F16) x = __half22float2(__floats2half2_rn(x.x, x.y));
+        else if (p.k_deq_dtype == DT_BF16) x = __bfloat1622float2(__floats2bfloat162_rn(x.x, x.y));
+        f[i] = x;
+      }
+    }
   }
 }
 
@@ -875,6 +900,8 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
             float2 a[D2], b[D2];
             Elem<KT>::template cvt2<DPT>(ts + (rg + RG * i2) * CF::ROWK + c * 16, a);
             Elem<KT>::template cvt2<DPT>(ts + (rg + RG * i2 + 32) * CF::ROWK + c * 16, b);
+            k_dequant<KT>(p, a);
+            k_dequant<KT>(p, b);
 #pragma unroll
             for (int d = 0; d < D2; ++d) {
               const float2 df = __ffma2_rn(b[d], f2(-1.f), a[d]);
@@ -987,6 +1014,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
             for (int m = 0; m < RPL; ++m) {
               float2 kk[D2];
               Elem<KT>::template cvt2<DPT>(ts + (rg + RG * m) * CF::ROWK + c * 16, kk);
+              k_dequant<KT>(p, kk);
 #pragma unroll
               for (int g = 0; g < GC; ++g) {
                 float2 acc = make_float2(0.f, 0.f);
@@ -1167,7 +1195,12 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       }
     }
   }
-  if (p.stats && lane == 0 && kept_stat) atomicAdd(p.stats, (uint32_t)kept_stat);
+  if constexpr (ATTN) {
+    // every team of the grid writes its count (no zeroing needed); merge_kernel sums them
+    if (p.team_kept != nullptr && panel == 0 && lane == 0) p.team_kept[wg] = kept_stat;
+  } else {
+    if (p.stats && lane == 0 && kept_stat) atomicAdd(p.stats, (uint32_t)kept_stat);
+  }
   // this CTA's decode work is issued: the merge grid may be scheduled (its
   // griddepcontrol.wait still waits for the whole grid to complete)
   if constexpr (ATTN) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1187,6 +1220,16 @@ __global__ void __launch_bounds__(128) merge_kernel(const DecodeParams p, int64_
   const int64_t item = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int nchunks = (p.group + GC - 1) / GC;
   const int U = p.num_seqs * p.num_kv_heads * nchunks;
+  if (p.stats != nullptr && blockIdx.x == 0 && threadIdx.x < 32) {  // retained-tile count of the launch
+    int s = 0;
+    for (int64_t i = lane; i < W; i += 32) s += __ldcg(p.team_kept + i);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) {
+      if (p.stats_add) *p.stats += (uint32_t)s;
+      else *p.stats = (uint32_t)s;
+    }
+  }
   if (item >= (int64_t)U * P) return;
   const int u = (int)(item / P), panel = (int)(item % P);
   const int* tp = p.tile_prefix;

@@ -31,5 +31,4 @@ int dispatch_f8_32(const DecodeParams& p, const TensorMaps& m, int v_dtype, int 
 int dispatch_f8_64(const DecodeParams& p, const TensorMaps& m, int v_dtype, int gc, bool attn, int num_sms, cudaStream_t st, bool tc);
 int dispatch_f8_128(const DecodeParams& p, const TensorMaps& m, int v_dtype, int gc, bool attn, int num_sms, cudaStream_t st, bool tc);
 int dispatch_f8_256(const DecodeParams& p, const TensorMaps& m, int v_dtype, int gc, bool attn, int num_sms, cudaStream_t st, bool tc);
-size_t workspace_header_bytes();
 }  // namespace oc

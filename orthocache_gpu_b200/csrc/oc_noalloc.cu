@@ -8,9 +8,9 @@
 // process exits.  In host code `g_scratch` only names the array: its device
 // address comes from cudaGetSymbolAddress, looked up once per device on the
 // first call with that device current (so make the first call before any
-// stream capture).  All calls share the array; its header is zeroed on the
-// stream before every launch, so a failed launch cannot poison the next one,
-// but calls that overlap on the GPU race.
+// stream capture).  Every launch writes the parts of the array it later
+// reads, so the array needs no clearing between calls; all calls share it,
+// so calls that overlap on the GPU race.
 #include <mutex>
 
 #include "../../include/orthocache_b200.h"
@@ -66,9 +66,6 @@ extern "C" int oc_fused_attention_v2_noalloc(const void* q, int q_dtype, int64_t
   void* ws = nullptr;
   const int r = scratch_address(&ws);
   if (r != OC_OK) return r;
-  const size_t zero = need < oc::workspace_header_bytes() ? need : oc::workspace_header_bytes();
-  if (zero > 0 && cudaMemsetAsync(ws, 0, zero, static_cast<cudaStream_t>(stream)) != cudaSuccess)
-    return OC_ERR_CUDA;
   return oc_fused_attention_v2(q, q_dtype, q_head_stride, keys, k_dtype, k_head_stride, k_tok_stride, values,
                                v_dtype, v_head_stride, v_tok_stride, num_heads, seq_len, head_dim, zeta_max,
                                splits, sms, out, out_dtype, out_head_stride, mask_out, retained, status, ws,

@@ -69,17 +69,16 @@ def shard_partials(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, ta
     m = torch.empty(hq, dtype=torch.float32, device=dev)
     l = torch.empty(hq, dtype=torch.float32, device=dev)
     acc = torch.empty((hq, head_dim), dtype=torch.float32, device=dev)
-    ws = _lib.workspace(dev)
-    wbuf = ws.get(lib.oc_workspace_bytes(num_kv_heads, G, num_tiles, head_dim))
-    if stats:
-        ws.ctrl[0].zero_()
+    stream = _lib.stream_ptr(dev)
+    ws = _lib.workspace(dev, stream)
+    wptr, wbytes = ws.get(_lib.workspace_bytes(num_kv_heads, G, num_tiles, head_dim))
     _lib.check(lib.oc_fused_attention_v3_shard(
         q.data_ptr(), _lib.dtype_code(q), q.stride(0),
         keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1),
         values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1),
         num_kv_heads, G, seq_len, head_dim, float(tau), num_splits, _lib.num_sms(dev),
-        m.data_ptr(), l.data_ptr(), acc.data_ptr(), 0, ws.ctrl.data_ptr() if stats else 0, ws.ctrl[1:].data_ptr(),
-        wbuf.data_ptr(), wbuf.numel(), _lib.stream_ptr(dev)), "oc_fused_attention_v3_shard")
+        m.data_ptr(), l.data_ptr(), acc.data_ptr(), 0, ws.retained_ptr if stats else 0, ws.status_ptr,
+        wptr, wbytes, stream), "oc_fused_attention_v3_shard")
     return m, l, acc, (_lib.read_stats(ws) if stats else -1)
 
 
@@ -127,15 +126,19 @@ def sequence_sharded_decode(q: torch.Tensor, keys_shard: torch.Tensor, values_sh
 
     Every rank passes the same q (Hq, hd) and its own tile-aligned shard
     (``shard_range``) of keys / values (KVH, S_shard, hd).  Returns the
-    output (Hq, hd) in q's dtype on every rank, and metadata with this rank's
-    retained-tile count.
+    output (Hq, hd) in q's dtype on every rank, and metadata.  Nothing is read
+    back to the host before the all-gather; a device error of this rank's
+    launch stays in the stream's status word (``check_status()``).
     """
     input_dtype = q.dtype
-    m, l, acc, kept = shard_partials(q, keys_shard, values_shard, tau, num_query_groups, num_splits, k_scale)
+    # no host synchronisation before the collective: the retained count is not read
+    # (the sticky status word stays checkable with check_status())
+    m, l, acc, kept = shard_partials(q, keys_shard, values_shard, tau, num_query_groups, num_splits, k_scale,
+                                     stats=False)
     gathered = gather_states(pack_state(m, l, acc), group)
     mm, ll, aa = unpack_for_merge(gathered)
     out = merge_states(mm, ll, aa, input_dtype)
     meta = {"layout": "sequence_sharded", "world_size": gathered.shape[0],
-            "shard_tiles": keys_shard.shape[1] // TILE_SIZE, "tiles_retained_local": kept,
+            "shard_tiles": keys_shard.shape[1] // TILE_SIZE,
             "gate_type": "cauchy_schwarz", "num_query_groups": num_query_groups}
     return out, meta

@@ -13,8 +13,10 @@ Differences from the reference, all additive:
 * keyword-only ``stats`` (default True): the metadata carries
   ``tiles_retained`` / ``tiles_evicted`` / ``eviction_rate`` (the reference's
   CPU-path keys) next to the GPU-path keys, read back with one synchronising
-  copy.  ``stats=False`` skips that read (no host synchronisation at all,
-  e.g. for CUDA-graph capture);
+  copy that also raises if the kernel reported an error.  ``stats=False``
+  skips that read (no host synchronisation at all, e.g. for CUDA-graph
+  capture) and puts the device status word in ``meta['status']`` instead;
+  ``check_status()`` raises on it later;
 * strided keys / values are streamed in place instead of being copied by
   ``.contiguous()`` when their rows are 16-byte aligned.
 """
@@ -33,15 +35,23 @@ def _auto_num_splits(num_tiles: int, device: torch.device) -> int:
     """The reference's split heuristic (fused_eviction.py:556-570)."""
     if device.type != "cuda":
         return 1
-    return _lib.load().oc_auto_num_splits(num_tiles, _lib.num_sms(device))
+    return _lib.auto_num_splits(num_tiles, device)
 
 
 def _finish_meta(meta: Dict[str, Any], ws, num_tiles_total: int, stats: bool) -> Dict[str, Any]:
+    """Add the counts (one synchronising read) or, with ``stats=False``, the device status word.
+
+    Without stats nothing is read back: ``meta['status']`` is the stream's
+    sticky status word on the device (0 = every launch so far was valid);
+    ``orthocache_gpu_b200.check_status()`` reads it and raises.
+    """
     if stats:
         kept = _lib.read_stats(ws)
         meta["tiles_retained"] = kept
         meta["tiles_evicted"] = num_tiles_total - kept
         meta["eviction_rate"] = (num_tiles_total - kept) / max(1, num_tiles_total)
+    else:
+        meta["status"] = ws.status
     return meta
 
 
@@ -90,20 +100,17 @@ def fused_orthocache_attention_v2(
     out = torch.empty((num_heads, head_dim), dtype=input_dtype, device=dev)
     mask = torch.empty((num_heads, num_tiles), dtype=torch.bool, device=dev) if return_mask else None
 
-    lib = _lib.load()
-    ws = _lib.workspace(dev)
-    wbytes = lib.oc_workspace_bytes(num_heads, 1, num_tiles, head_dim)
-    wbuf = ws.get(wbytes)
-    if stats:
-        ws.ctrl[0].zero_()
-    _lib.check(lib.oc_fused_attention_v2(
+    stream = _lib.stream_ptr(dev)
+    ws = _lib.workspace(dev, stream)
+    wptr, wbytes = ws.get(_lib.workspace_bytes(num_heads, 1, num_tiles, head_dim))
+    _lib.check(_lib.load().oc_fused_attention_v2(
         q.data_ptr(), _lib.dtype_code(q), q.stride(0),
         keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1),
         values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1),
         num_heads, seq_len, head_dim, float(zeta_max), num_splits, _lib.num_sms(dev),
         out.data_ptr(), _lib.dtype_code(out), out.stride(0),
-        _lib.ptr(mask), ws.ctrl.data_ptr() if stats else 0, ws.ctrl[1:].data_ptr(),
-        wbuf.data_ptr(), wbuf.numel(), _lib.stream_ptr(dev)), "fused_orthocache_attention_v2")
+        _lib.ptr(mask), ws.retained_ptr if stats else 0, ws.status_ptr,
+        wptr, wbytes, stream), "fused_orthocache_attention_v2")
 
     meta: Dict[str, Any] = {
         "num_splits": num_splits,
@@ -153,20 +160,17 @@ def fused_orthocache_attention(
     out = torch.empty((1, head_dim), dtype=input_dtype, device=dev)
     mask = torch.empty(num_tiles, dtype=torch.bool, device=dev) if return_mask else None
 
-    lib = _lib.load()
-    ws = _lib.workspace(dev)
-    splits = lib.oc_auto_num_splits(num_tiles, _lib.num_sms(dev))
-    wbuf = ws.get(lib.oc_workspace_bytes(1, 1, num_tiles, head_dim))
-    if stats:
-        ws.ctrl[0].zero_()
-    _lib.check(lib.oc_fused_attention_v1(
+    stream = _lib.stream_ptr(dev)
+    ws = _lib.workspace(dev, stream)
+    wptr, wbytes = ws.get(_lib.workspace_bytes(1, 1, num_tiles, head_dim))
+    _lib.check(_lib.load().oc_fused_attention_v1(
         q.data_ptr(), _lib.dtype_code(q),
         keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0),
         values.data_ptr(), _lib.dtype_code(values), values.stride(0),
         num_tokens, head_dim, float(zeta_max), _lib.num_sms(dev),
         out.data_ptr(), _lib.dtype_code(out),
-        _lib.ptr(mask), ws.ctrl.data_ptr() if stats else 0, ws.ctrl[1:].data_ptr(),
-        wbuf.data_ptr(), wbuf.numel(), _lib.stream_ptr(dev)), "fused_orthocache_attention")
+        _lib.ptr(mask), ws.retained_ptr if stats else 0, ws.status_ptr,
+        wptr, wbytes, stream), "fused_orthocache_attention")
 
     meta: Dict[str, Any] = {}
     if return_mask:

@@ -66,9 +66,9 @@ def triton_fwht_eviction(
     keys = _lib.prepare_kv(keys)
     mask = torch.empty(num_tiles, dtype=torch.bool, device=dev)
     zeta = torch.empty(num_tiles, dtype=torch.float32, device=dev) if return_zeta else None
-    ws = _lib.workspace(dev)
-    lib = _lib.load()
-    _lib.check(lib.oc_fwht_eviction(keys.data_ptr(), _lib.dtype_code(keys), num_tokens, head_dim, keys.stride(0),
+    stream = _lib.stream_ptr(dev)
+    ws = _lib.workspace(dev, stream)
+    _lib.check(_lib.load().oc_fwht_eviction(keys.data_ptr(), _lib.dtype_code(keys), num_tokens, head_dim, keys.stride(0),
                                     float(zeta_max), mask.data_ptr(), _lib.ptr(zeta),
-                                    ws.ctrl[1:].data_ptr(), _lib.stream_ptr(dev)), "triton_fwht_eviction")
+                                    ws.status_ptr, stream), "triton_fwht_eviction")
     return mask, zeta

@@ -81,19 +81,17 @@ def fused_orthocache_attention_v3_gqa(
     out = torch.empty((num_seqs, num_query_heads, head_dim), dtype=input_dtype, device=dev)
     mask = torch.empty((num_seqs, num_kv_heads, num_tiles), dtype=torch.bool, device=dev) if return_mask else None
 
-    lib = _lib.load()
-    ws = _lib.workspace(dev)
-    wbuf = ws.get(lib.oc_workspace_bytes(num_seqs * num_kv_heads, G, num_tiles, head_dim))
-    if stats:
-        ws.ctrl[0].zero_()
-    _lib.check(lib.oc_fused_attention_v3_gqa(
+    stream = _lib.stream_ptr(dev)
+    ws = _lib.workspace(dev, stream)
+    wptr, wbytes = ws.get(_lib.workspace_bytes(num_seqs * num_kv_heads, G, num_tiles, head_dim))
+    _lib.check(_lib.load().oc_fused_attention_v3_gqa(
         q.data_ptr(), _lib.dtype_code(q), q.stride(0), q.stride(1),
         keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1), keys.stride(2),
         values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1), values.stride(2),
         num_seqs, num_kv_heads, G, seq_len, head_dim, float(tau), num_splits, _lib.num_sms(dev),
         out.data_ptr(), _lib.dtype_code(out), out.stride(0), out.stride(1),
-        _lib.ptr(mask), ws.ctrl.data_ptr() if stats else 0, ws.ctrl[1:].data_ptr(),
-        wbuf.data_ptr(), wbuf.numel(), _lib.stream_ptr(dev)), "fused_orthocache_attention_v3_gqa")
+        _lib.ptr(mask), ws.retained_ptr if stats else 0, ws.status_ptr,
+        wptr, wbytes, stream), "fused_orthocache_attention_v3_gqa")
 
     if not batched:
         out = out[0]

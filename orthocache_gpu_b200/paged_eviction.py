@@ -16,8 +16,11 @@ MHA, ζ-gated, fixed-length path.  Additive keyword-only extensions:
 * ``tau``: use the V3 Cauchy-Schwarz gate with this threshold instead of ζ;
 * ``return_mask``, ``stats`` as in V2.
 
-float8 key caches are read natively with ``k_scale`` folded into q (the
-reference de-quantises the whole cache on the host first, paged_eviction.py:355-357).
+float8 key caches are read natively (one byte a key element) and each
+element is de-quantised in registers exactly as the reference's host-side
+``k_cache.to(q.dtype) * k_scale`` would round it (paged_eviction.py:355-357),
+so the gate and the logits see the same keys; the reference materialises a
+de-quantised copy of the whole cache instead.
 """
 
 from __future__ import annotations
@@ -72,7 +75,12 @@ def fused_orthocache_attention_paged(
     group = num_heads // num_kv_heads
 
     input_dtype = q.dtype
-    if k_scale != 1.0:
+    fp8_keys = k_cache.dtype == torch.float8_e4m3fn
+    # float8 keys are de-quantised into q's dtype inside the kernel
+    # (round(k * k_scale) per element, paged_eviction.py:355-357); other
+    # dtypes fold k_scale into q like the reference
+    deq_scale = float(k_scale) if fp8_keys else 1.0
+    if k_scale != 1.0 and not fp8_keys:
         q = q * k_scale
     dev = _lib.require_cuda(q, k_cache, v_cache, block_tables)
     if num_splits is None:
@@ -90,24 +98,23 @@ def fused_orthocache_attention_paged(
         sl = seq_lens.to(device=dev, dtype=torch.int32).contiguous()
         assert sl.numel() == num_seqs, "seq_lens must have one entry per sequence"
     out = torch.empty((num_seqs, num_heads, head_dim), dtype=input_dtype, device=dev)
-    mask = torch.empty((num_seqs, num_kv_heads, num_tiles), dtype=torch.bool, device=dev) if return_mask else None
+    # tiles beyond a sequence's length are never gated: they read False (evicted)
+    mask = torch.zeros((num_seqs, num_kv_heads, num_tiles), dtype=torch.bool, device=dev) if return_mask else None
 
-    lib = _lib.load()
-    ws = _lib.workspace(dev)
-    wbuf = ws.get(lib.oc_workspace_bytes(num_seqs * num_kv_heads, group, num_tiles, head_dim))
-    if stats:
-        ws.ctrl[0].zero_()
+    stream = _lib.stream_ptr(dev)
+    ws = _lib.workspace(dev, stream)
+    wptr, wbytes = ws.get(_lib.workspace_bytes(num_seqs * num_kv_heads, group, num_tiles, head_dim))
     gate = _lib.OC_GATE_ZETA if tau is None else _lib.OC_GATE_CAUCHY_SCHWARZ
     thr = float(zeta_max) if tau is None else float(tau)
-    _lib.check(lib.oc_fused_attention_paged(
+    _lib.check(_lib.load().oc_fused_attention_paged(
         q.data_ptr(), _lib.dtype_code(q), q.stride(0), q.stride(1),
         k_cache.data_ptr(), _lib.dtype_code(k_cache), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
         v_cache.data_ptr(), _lib.dtype_code(v_cache), v_cache.stride(0), v_cache.stride(1), v_cache.stride(2),
         num_physical_blocks, block_size, bt.data_ptr(), bt.stride(0), max_blocks_per_seq, _lib.ptr(sl),
-        num_seqs, num_kv_heads, group, head_dim, gate, thr, num_splits, _lib.num_sms(dev),
+        num_seqs, num_kv_heads, group, head_dim, gate, thr, deq_scale, num_splits, _lib.num_sms(dev),
         out.data_ptr(), _lib.dtype_code(out), out.stride(0), out.stride(1),
-        _lib.ptr(mask), ws.ctrl.data_ptr() if stats else 0, ws.ctrl[1:].data_ptr(),
-        wbuf.data_ptr(), wbuf.numel(), _lib.stream_ptr(dev)), "fused_orthocache_attention_paged")
+        _lib.ptr(mask), ws.retained_ptr if stats else 0, ws.status_ptr,
+        wptr, wbytes, stream), "fused_orthocache_attention_paged")
 
     meta: Dict[str, Any] = {
         "num_splits": num_splits,
@@ -125,4 +132,6 @@ def fused_orthocache_attention_paged(
         if sl is not None:
             total = int((sl // tile_size).clamp(max=num_tiles).sum().item()) * num_kv_heads
         _finish_meta(meta, ws, total, True)
+    else:
+        meta["status"] = ws.status
     return out, meta

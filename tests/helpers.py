@@ -20,6 +20,8 @@ def golden(name):
 
 
 def as_np(t):
+    if isinstance(t, np.ndarray):
+        return t
     return t.detach().float().cpu().numpy()
 
 
@@ -42,3 +44,10 @@ def assert_mask(mask, keep_ref, score_ref, thr, what=""):
     bad = (m != keep_ref) & ~near
     assert not bad.any(), f"{what}: {int(bad.sum())} mask mismatches outside the near-threshold list"
     return np.argwhere(near)
+
+
+def gpu_forced(mask, score_ref, thr):
+    """(where, keep) for the oracle's ``forced`` argument: the GPU's decisions
+    on the near-threshold tiles (where either decision is correct), so that
+    outputs and counts can be compared exactly in every case."""
+    return orc.near_threshold(score_ref, thr, NEAR_REL), as_np(mask).astype(bool)

@@ -7,6 +7,7 @@ GPU: the CUDA shard kernel and the CUDA log-sum-exp merge, with the ranks
 emulated on one GPU (and over NCCL when two GPUs are visible).
 """
 
+import datetime
 import os
 import socket
 
@@ -73,7 +74,7 @@ def _free_port():
 
 def _gloo_rank(rank, world, port, result):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         inp = _inputs()
         a, b = ocd.shard_range(SEQ, world, rank)
@@ -119,7 +120,7 @@ def test_gpu_shards_merged_on_one_gpu_match_v3(world):
 def _nccl_rank(rank, world, port, result):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         inp = _inputs()
         q, k, v = inp.torch(torch.bfloat16, f"cuda:{rank}")

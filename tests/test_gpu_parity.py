@@ -12,7 +12,7 @@ import torch
 
 import orthocache_gpu_b200 as oc
 from cases import case_inputs, fp8_quantize
-from helpers import as_np, assert_close, assert_mask, cast_np, golden
+from helpers import as_np, assert_close, assert_mask, cast_np, golden, gpu_forced
 from oracle import orthocache_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -52,9 +52,14 @@ def test_v1_config1_matches_reference_golden():
                                                   return_mask=True)
         assert out.shape == (1, 128) and out.dtype == torch.float32
         near = assert_mask(meta["eviction_mask"], z[f"mask_{i}"], zeta, thr, "v1")
-        if len(near) == 0:
+        if len(near) == 0:  # the reference's own output applies
             assert meta["tiles_retained"] == int(z[f"retained_{i}"])
             assert_close(out, z[f"out_{i}"], torch.float32, f"v1 thr={thr}")
+        else:  # the oracle with the GPU's decisions on the listed tiles
+            ref, rm = orc.v1_attention(inp["q"], inp["keys"], inp["values"], thr,
+                                       forced=gpu_forced(meta["eviction_mask"], zeta, thr))
+            assert meta["tiles_retained"] == rm["tiles_retained"]
+            assert_close(out, ref, torch.float32, f"v1 thr={thr} (near tiles forced)")
 
 
 @pytest.mark.parametrize("name", ["v2_f16", "v2_bf16_hd64"])
@@ -110,9 +115,10 @@ def _v2_case(h, s, hd, dt, thr, seed, splits=None):
     out, gm = oc.fused_orthocache_attention_v2(T(x.q, dt), T(x.keys, dt), T(x.values, dt), thr,
                                                num_splits=splits, return_mask=True)
     near = assert_mask(gm["eviction_mask"], meta["eviction_mask"], meta["zeta"], thr, "v2 mask")
-    if len(near) == 0:
-        assert gm["tiles_retained"] == meta["tiles_retained"]
-        assert_close(out, ref, dt, f"v2 h={h} s={s} hd={hd} {dt}")
+    if len(near):
+        ref, meta = orc.v2_attention(q, k, v, thr, forced=gpu_forced(gm["eviction_mask"], meta["zeta"], thr))
+    assert gm["tiles_retained"] == meta["tiles_retained"]
+    assert_close(out, ref, dt, f"v2 h={h} s={s} hd={hd} {dt}")
     return gm
 
 
@@ -201,9 +207,11 @@ def test_v3_groups(group):
         out, gm = oc.fused_orthocache_attention_v3_gqa(T(x.q, dt), T(x.keys, dt), T(x.values, dt), tau, group,
                                                        return_mask=True)
         near = assert_mask(gm["eviction_mask"], meta["eviction_mask"], meta["cs_bound"], tau, "v3")
-        if len(near) == 0:
-            assert gm["tiles_retained"] == meta["tiles_retained"]
-            assert_close(out, ref, dt, f"v3 G={group} tau={tau}")
+        if len(near):
+            ref, meta = orc.v3_gqa_attention(q, k, v, tau, group,
+                                             forced=gpu_forced(gm["eviction_mask"], meta["cs_bound"], tau))
+        assert gm["tiles_retained"] == meta["tiles_retained"]
+        assert_close(out, ref, dt, f"v3 G={group} tau={tau}")
 
 
 def test_v3_batched_extension_equals_per_sequence_calls():
@@ -225,12 +233,26 @@ def test_paged_gqa_ragged_against_composed_oracle(block_size):
     x = paged_inputs(5, 2, 4, 128, block_size, 64, 1024, seed=block_size, extra_blocks=3)
     dt = torch.float16
     q, kc, vc, bt, sl = x.torch(dt, DEV)
-    ref, keep = orc.paged_attention(cast_np(x.q, dt), cast_np(x.k_cache, dt), cast_np(x.v_cache, dt),
-                                    x.block_tables, tau=150.0, seq_lens=x.seq_lens)
+    args = (cast_np(x.q, dt), cast_np(x.k_cache, dt), cast_np(x.v_cache, dt), x.block_tables)
+    ref, keep, score = orc.paged_attention(*args, tau=150.0, seq_lens=x.seq_lens)
     out, meta = oc.fused_orthocache_attention_paged(q, kc, vc, bt, None, seq_lens=sl, tau=150.0,
                                                     return_mask=True)
+    _check_paged_mask(meta["eviction_mask"], keep, score, 150.0, x.seq_lens, f"paged bs={block_size}")
+    if orc.near_threshold(score, 150.0).any():
+        ref, keep, _ = orc.paged_attention(*args, tau=150.0, seq_lens=x.seq_lens,
+                                           forced=gpu_forced(meta["eviction_mask"], score, 150.0))
     assert meta["tiles_retained"] == int(keep.sum())
     assert_close(out, ref, dt, f"paged bs={block_size}")
+
+
+def _check_paged_mask(mask, keep, score, thr, seq_lens, what):
+    """Bit-exact on every valid tile (outside the near list); False beyond each sequence's length."""
+    m = as_np(mask).astype(bool)
+    valid = np.zeros(keep.shape, bool)
+    for s_, n in enumerate(seq_lens):
+        valid[s_, :, : int(n) // 64] = True
+    assert not (m & ~valid).any(), f"{what}: mask set beyond a sequence's length"
+    assert_mask(m[valid], keep[valid], score[valid], thr, what)
 
 
 def test_paged_mha_zeta_equals_v2_per_sequence():
@@ -239,8 +261,13 @@ def test_paged_mha_zeta_equals_v2_per_sequence():
     dt = torch.float16
     q, kc, vc, bt, _ = x.torch(dt, DEV)
     out, _ = oc.fused_orthocache_attention_paged(q, kc, vc, bt, 1.0)
-    ref, _ = orc.paged_attention(cast_np(x.q, dt), cast_np(x.k_cache, dt), cast_np(x.v_cache, dt),
-                                 x.block_tables, zeta_max=1.0)
+    args = (cast_np(x.q, dt), cast_np(x.k_cache, dt), cast_np(x.v_cache, dt), x.block_tables)
+    _, gm = oc.fused_orthocache_attention_paged(q, kc, vc, bt, 1.0, return_mask=True)
+    ref, keep, score = orc.paged_attention(*args, zeta_max=1.0)
+    assert_mask(gm["eviction_mask"], keep, score, 1.0, "paged mha zeta mask")
+    if orc.near_threshold(score, 1.0).any():
+        ref, keep, _ = orc.paged_attention(*args, zeta_max=1.0, forced=gpu_forced(gm["eviction_mask"], score, 1.0))
+    assert gm["tiles_retained"] == int(keep.sum())
     assert_close(out, ref, dt, "paged mha zeta")
 
 
@@ -269,9 +296,92 @@ def test_paged_batch_with_an_empty_sequence():
     dt = torch.float16
     q, kc, vc, bt, _ = x.torch(dt, DEV)
     sl = torch.from_numpy(lens).to(DEV)
-    ref, keep = orc.paged_attention(cast_np(x.q, dt), cast_np(x.k_cache, dt), cast_np(x.v_cache, dt),
-                                    x.block_tables, tau=150.0, seq_lens=lens)
-    out, meta = oc.fused_orthocache_attention_paged(q, kc, vc, bt, None, seq_lens=sl, tau=150.0)
+    args = (cast_np(x.q, dt), cast_np(x.k_cache, dt), cast_np(x.v_cache, dt), x.block_tables)
+    ref, keep, score = orc.paged_attention(*args, tau=150.0, seq_lens=lens)
+    out, meta = oc.fused_orthocache_attention_paged(q, kc, vc, bt, None, seq_lens=sl, tau=150.0, return_mask=True)
+    _check_paged_mask(meta["eviction_mask"], keep, score, 150.0, lens, "paged with an empty sequence")
+    if orc.near_threshold(score, 150.0).any():
+        ref, keep, _ = orc.paged_attention(*args, tau=150.0, seq_lens=lens,
+                                           forced=gpu_forced(meta["eviction_mask"], score, 150.0))
     assert meta["tiles_retained"] == int(keep.sum())
     assert out[1].abs().max().item() == 0.0
     assert_close(out, ref, dt, "paged with an empty sequence")
+
+
+# ------------------------------------------------------------ float8 keys
+# The reference's fp8 path (tests/test_fp8.py:33-127): keys quantised with
+# scale = max|k| / 448, k_scale folded into q for V1 / V2 / V3; the paged path
+# de-quantises the cache into q's dtype first (paged_eviction.py:355-357).
+def _q_scaled(q32, scale):
+    return (torch.from_numpy(np.ascontiguousarray(q32)) * scale).numpy()
+
+
+@pytest.mark.parametrize("thr", [999.0, 1.0])
+def test_fp8_keys_v1(thr):
+    from orthocache_gpu_b200.synthetic import mha_inputs
+    x = mha_inputs(1, 2048, 128, seed=31)
+    k8, s = fp8_quantize(x.keys[0])
+    out, meta = oc.fused_orthocache_attention(T(x.q), k8.to(DEV), T(x.values[0]), thr, return_mask=True, k_scale=s)
+    kf = k8.float().numpy()
+    ref, rm = orc.v1_attention(_q_scaled(x.q, s), kf, x.values[0], thr)
+    assert_mask(meta["eviction_mask"], rm["eviction_mask"], rm["zeta"], thr, "v1 fp8")
+    ref, rm = orc.v1_attention(_q_scaled(x.q, s), kf, x.values[0], thr,
+                               forced=gpu_forced(meta["eviction_mask"], rm["zeta"], thr))
+    assert meta["tiles_retained"] == rm["tiles_retained"]
+    assert_close(out, ref, torch.float32, f"v1 fp8 thr={thr}")
+
+
+@pytest.mark.parametrize("tau", [999.0, 150.0])
+def test_fp8_keys_v3(tau):
+    from orthocache_gpu_b200.synthetic import gqa_inputs
+    x = gqa_inputs(2, 4, 1024, 128, seed=32)
+    k8, s = fp8_quantize(x.keys)
+    out, meta = oc.fused_orthocache_attention_v3_gqa(T(x.q), k8.to(DEV), T(x.values), tau, 4, return_mask=True,
+                                                     k_scale=s)
+    kf, qs = k8.float().numpy(), _q_scaled(x.q, s)
+    ref, rm = orc.v3_gqa_attention(qs, kf, x.values, tau, 4)
+    assert_mask(meta["eviction_mask"], rm["eviction_mask"], rm["cs_bound"], tau, "v3 fp8")
+    ref, rm = orc.v3_gqa_attention(qs, kf, x.values, tau, 4,
+                                   forced=gpu_forced(meta["eviction_mask"], rm["cs_bound"], tau))
+    assert meta["tiles_retained"] == rm["tiles_retained"]
+    assert_close(out, ref, torch.float32, f"v3 fp8 tau={tau}")
+
+
+@pytest.mark.parametrize("qdt", [torch.float16, torch.bfloat16, torch.float32])
+def test_fp8_keys_paged_dequantise_into_q_dtype(qdt):
+    # reference semantics: K_eff = (k8.to(q.dtype) * k_scale) in q's dtype, q unscaled;
+    # tolerance: the query dtype's (1e-5 float32, 2e-3 float16 / bfloat16)
+    from orthocache_gpu_b200.synthetic import paged_inputs
+    x = paged_inputs(4, 2, 4, 128, 16, 256, 1024, seed=33)
+    k8, s = fp8_quantize(x.k_cache)
+    keff = (k8.to(qdt) * s).float().numpy()
+    q, _, vc, bt, sl = x.torch(qdt, DEV)
+    out, meta = oc.fused_orthocache_attention_paged(q, k8.to(DEV), vc, bt, None, seq_lens=sl, tau=150.0,
+                                                    return_mask=True, k_scale=s)
+    args = (cast_np(x.q, qdt), keff, cast_np(x.v_cache, qdt), x.block_tables)
+    ref, keep, score = orc.paged_attention(*args, tau=150.0, seq_lens=x.seq_lens)
+    _check_paged_mask(meta["eviction_mask"], keep, score, 150.0, x.seq_lens, f"paged fp8 {qdt}")
+    ref, keep, _ = orc.paged_attention(*args, tau=150.0, seq_lens=x.seq_lens,
+                                       forced=gpu_forced(meta["eviction_mask"], score, 150.0))
+    assert meta["tiles_retained"] == int(keep.sum())
+    assert_close(out, ref, qdt, f"paged fp8 {qdt}")
+
+
+# ------------------------------------------------------------ device status without a host read
+def test_bad_block_table_entry_is_reported_with_stats_false():
+    # an out-of-range page id: the kernel clamps the lookup to page 0 (no bad
+    # access) and sets a status bit; a stats=False call cannot raise itself,
+    # so the bit is visible in meta['status'] and raised by check_status()
+    from orthocache_gpu_b200.synthetic import paged_inputs
+    x = paged_inputs(2, 2, 1, 64, 16, 128, 256, seed=3)
+    q, kc, vc, bt, _ = x.torch(torch.float16, DEV)
+    oc.check_status()
+    bt[0, 0] = kc.shape[0] + 5
+    out, meta = oc.fused_orthocache_attention_paged(q, kc, vc, bt, 1.0, stats=False)
+    assert int(meta["status"].item()) & 2
+    with pytest.raises(RuntimeError, match="block-table"):
+        oc.check_status()
+    oc.check_status()  # the word was cleared by the read
+    bt[0, 0] = -1
+    with pytest.raises(RuntimeError, match="block-table"):
+        oc.fused_orthocache_attention_paged(q, kc, vc, bt, 1.0)  # stats=True raises at once

@@ -86,7 +86,7 @@ def test_v3_matches_reference(name):
 def test_paged_matches_reference():
     inp, z = load("paged_f32")
     for i, thr in enumerate(z["thresholds"]):
-        out, _ = orc.paged_attention(inp["q"], inp["k_cache"], inp["v_cache"],
+        out, _, _ = orc.paged_attention(inp["q"], inp["k_cache"], inp["v_cache"],
                                      inp["block_tables"], zeta_max=thr)
         np.testing.assert_allclose(out, z[f"out_{i}"], atol=1e-6, rtol=0)
 
