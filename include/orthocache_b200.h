@@ -174,6 +174,59 @@ int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_strid
                                 float* l_out, float* acc_out, uint8_t* mask_out, uint32_t* retained,
                                 uint32_t* status, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- spectral norm cache and the O(1) decode gate ----------------------
+ * Reference: src/orthocache_gpu/norm_cache.py:21-146 (SpectralNormCache),
+ * triton_kernels/decode_gate.py:54-300 (compute_q_high_norm_exact,
+ * decode_gate, _pytorch_decode_gate), eval/perplexity_eval.py:554-674 (the
+ * decode path that consumes them). */
+
+/* Per 64-token tile of each head: |(W K_tile)[high_start:high_end]|_F, W the
+ * natural-order 64-point Walsh matrix / 8 applied along the tokens, norms
+ * below 1e-38 written as 0 (norm_cache.py:58-88 update_prefill).  keys
+ * (num_heads, num_tokens, head_dim) with element strides; out[h *
+ * out_head_stride + t].  Replaces SpectralNormCache.update_prefill /
+ * populate_from_keys (norm_cache.py:58-117); the default band of the
+ * reference's model path is [48, 64) (eval/perplexity_eval.py:436). */
+int oc_tile_high_norms(const void* keys, int k_dtype, int num_heads, int64_t num_tokens, int head_dim,
+                       int64_t k_head_stride, int64_t k_tok_stride, int high_start, int high_end, float* out,
+                       int64_t out_head_stride, void* stream);
+
+/* Decode gate (decode_gate.py:188-300).  q (num_kv_heads*group, head_dim);
+ * norms (num_kv_heads, >= max_tiles) float32 with norm_head_stride.  Per kv
+ * head s = max (q_stat 0) or sorted(...)[group/2] (q_stat 1, the model
+ * path's median, perplexity_eval.py:612-616) over its query heads of
+ * |q_high|_2 = sqrt(max(0, |q|^2 - sum_i S_i^2 / bs)) with S_i the sums of
+ * low_band contiguous blocks of bs = head_dim/low_band dims (tight = 1,
+ * compute_q_high_norm_exact) or |q|_2 (tight = 0).  evict_out (nullable,
+ * (num_kv_heads, max_tiles) bytes): 1 iff float32(s * norm[t]) <=
+ * float32(tau * 64 * head_dim) for t < num_tiles, 0 beyond.  q_norms_out
+ * (nullable): s per kv head. */
+int oc_decode_gate(const void* q, int q_dtype, int64_t q_head_stride, int num_kv_heads, int group, int head_dim,
+                   const float* norms, int64_t norm_head_stride, int num_tiles, int max_tiles, double tau,
+                   int tight, int low_band, int q_stat, uint8_t* evict_out, float* q_norms_out, void* stream);
+
+/* Bytes of workspace for oc_fused_attention_cached. */
+size_t oc_cached_workspace_bytes(int64_t num_groups, int group, int64_t num_tiles, int head_dim);
+
+/* Decode attention gated by cached key norms: oc_decode_gate (low_band 8)
+ * per (sequence, kv head), then attention over the retained tiles only --
+ * an evicted tile costs no K and no V read.  Shapes as
+ * oc_fused_attention_v3_gqa; norms (num_seqs, num_kv_heads, >= seq_len/64)
+ * with element strides.  evict_out (nullable, (num_seqs, num_kv_heads,
+ * seq_len/64)): the gate's evict flags.  The reference evaluates this gate
+ * and masks the logits of the dense product (perplexity_eval.py:554-674);
+ * the output is the same softmax over the retained tiles. */
+int oc_fused_attention_cached(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                              const void* keys, int k_dtype, int64_t k_seq_stride, int64_t k_head_stride,
+                              int64_t k_tok_stride, const void* values, int v_dtype, int64_t v_seq_stride,
+                              int64_t v_head_stride, int64_t v_tok_stride, int num_seqs, int num_kv_heads,
+                              int group, int64_t seq_len, int head_dim, const float* norms,
+                              int64_t norm_seq_stride, int64_t norm_head_stride, double tau, int tight,
+                              int q_stat, int num_sms, void* out, int out_dtype, int64_t out_seq_stride,
+                              int64_t out_head_stride, uint8_t* evict_out, float* q_norms_out,
+                              uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
 /* Allocation-free variant of oc_fused_attention_v2 (no counterpart in the
  * reference).  For callers that cannot allocate device memory: code running
  * inside another framework's allocator, under a memory budget, or from a

@@ -19,8 +19,16 @@ from .fwht_fused_prototype import (
     generate_walsh_matrix,
     triton_fwht_eviction,
 )
+from .decode_gate import (
+    apply_decode_mask,
+    apply_decode_mask_vectorized,
+    compute_q_high_norm_exact,
+    decode_gate,
+    fused_orthocache_attention_cached,
+)
 from .gqa_eviction import fused_orthocache_attention_v3_gqa
 from .paged_eviction import fused_orthocache_attention_paged
+from .norm_cache import SpectralNormCache, create_norm_cache_for_model, tile_high_norms
 from .pipeline import BypassFlag, GPUProfile, TelemetryLevel, format_bypass_reason, orthocache_forward
 
 __version__ = "0.1.0"
@@ -38,6 +46,14 @@ __all__ = [
     "GPUProfile",
     "format_bypass_reason",
     "check_status",
+    "decode_gate",
+    "compute_q_high_norm_exact",
+    "apply_decode_mask",
+    "apply_decode_mask_vectorized",
+    "fused_orthocache_attention_cached",
+    "SpectralNormCache",
+    "create_norm_cache_for_model",
+    "tile_high_norms",
     "TILE_SIZE",
     "BAND_DC_64",
     "BAND_LOW_64",

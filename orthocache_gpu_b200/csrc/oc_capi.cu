@@ -353,6 +353,10 @@ static int v3_common(DecodeParams& p, const void* q, int q_dtype, int64_t q_seq_
     if (out) pc.out = static_cast<char*>(out) + s0 * out_seq_stride * osz;
     if (p.mask) pc.mask = p.mask + s0 * num_kv_heads * tiles;
     pc.stats_add = s0 > 0 ? 1 : 0;  // the first launch sets the count, later ones add
+    if (p.tile_list) {
+      pc.tile_list = p.tile_list + s0 * num_kv_heads * p.list_stride;
+      pc.list_count = p.list_count + s0 * num_kv_heads;
+    }
     const int r = attach_workspace(pc, ns * units_per_seq, head_dim, workspace, workspace_bytes);
     if (r != OC_OK) return r;
     const int e = run(pc, k_dtype, v_dtype, head_dim, true, sms, static_cast<cudaStream_t>(stream));
@@ -471,6 +475,120 @@ int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, i
                    v_cache, v_dtype, 0, v_head_stride, v_tok_stride, num_seqs, num_kv_heads, group, seq_len,
                    head_dim, num_splits, num_sms, out, out_dtype, out_seq_stride, out_head_stride, mask_out,
                    retained, status, workspace, workspace_bytes, stream);
+}
+
+namespace {
+// bytes after the regular workspace: per-(sequence, kv head) counts, then the tile lists
+size_t cached_extra(int64_t groups, int64_t tiles) { return pad256(4 * (size_t)groups) + pad256(4 * (size_t)groups * tiles); }
+}  // namespace
+
+size_t oc_cached_workspace_bytes(int64_t num_groups, int group, int64_t num_tiles, int head_dim) {
+  const size_t b = oc_workspace_bytes(num_groups, group, num_tiles, head_dim);
+  return b == 0 ? 0 : b + cached_extra(num_groups, num_tiles);
+}
+
+int oc_tile_high_norms(const void* keys, int k_dtype, int num_heads, int64_t num_tokens, int head_dim,
+                       int64_t k_head_stride, int64_t k_tok_stride, int high_start, int high_end, float* out,
+                       int64_t out_head_stride, void* stream) {
+  if (!keys || !out || num_heads < 0 || num_tokens < 0 || (num_tokens % 64) != 0) return OC_ERR_INVALID;
+  if (elem_bytes(k_dtype) == 0) return OC_ERR_UNSUPPORTED;
+  if (head_dim < 1 || head_dim > 256) return OC_ERR_UNSUPPORTED;
+  if (high_start < 0 || high_end > 64 || high_start > high_end) return OC_ERR_INVALID;
+  if (num_tokens / 64 > INT32_MAX) return OC_ERR_INVALID;
+  return oc::launch_tile_high_norms(keys, k_dtype, num_heads, (int)(num_tokens / 64), head_dim, k_head_stride,
+                                    k_tok_stride, high_start, high_end, out, out_head_stride,
+                                    static_cast<cudaStream_t>(stream));
+}
+
+static float gate_threshold(double tau, int head_dim) {
+  // torch compares the float32 bounds with the Python scalar tau * (64 * head_dim) cast to float32
+  return static_cast<float>(tau * (64.0 * head_dim));
+}
+
+int oc_decode_gate(const void* q, int q_dtype, int64_t q_head_stride, int num_kv_heads, int group, int head_dim,
+                   const float* norms, int64_t norm_head_stride, int num_tiles, int max_tiles, double tau,
+                   int tight, int low_band, int q_stat, uint8_t* evict_out, float* q_norms_out, void* stream) {
+  if (!q || !norms || num_kv_heads < 1 || group < 1 || group > 64 || head_dim < 1 || num_tiles < 0 ||
+      max_tiles < num_tiles || low_band < 1 || low_band > 32 || (tight && head_dim % low_band))
+    return OC_ERR_INVALID;
+  if (q_dtype != OC_F32 && q_dtype != OC_F16 && q_dtype != OC_BF16) return OC_ERR_UNSUPPORTED;
+  oc::GateArgs a{};
+  a.q = q;
+  a.q_dtype = q_dtype;
+  a.q_head_stride = q_head_stride;
+  a.num_seqs = 1;
+  a.num_kv_heads = num_kv_heads;
+  a.group = group;
+  a.head_dim = head_dim;
+  a.norms = norms;
+  a.norm_head_stride = norm_head_stride;
+  a.num_tiles = num_tiles;
+  a.max_tiles = max_tiles;
+  a.thr = gate_threshold(tau, head_dim);
+  a.tight = tight;
+  a.low_band = low_band;
+  a.stat_median = q_stat;
+  a.evict = evict_out;
+  a.evict_stride = max_tiles;
+  a.q_norms = q_norms_out;
+  return oc::launch_decode_gate(a, static_cast<cudaStream_t>(stream));
+}
+
+int oc_fused_attention_cached(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                              const void* keys, int k_dtype, int64_t k_seq_stride, int64_t k_head_stride,
+                              int64_t k_tok_stride, const void* values, int v_dtype, int64_t v_seq_stride,
+                              int64_t v_head_stride, int64_t v_tok_stride, int num_seqs, int num_kv_heads,
+                              int group, int64_t seq_len, int head_dim, const float* norms,
+                              int64_t norm_seq_stride, int64_t norm_head_stride, double tau, int tight,
+                              int q_stat, int num_sms, void* out, int out_dtype, int64_t out_seq_stride,
+                              int64_t out_head_stride, uint8_t* evict_out, float* q_norms_out,
+                              uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  if (!norms || num_seqs < 1 || num_kv_heads < 1 || group < 1 || group > 64 || seq_len < 0 || (seq_len % 64))
+    return OC_ERR_INVALID;
+  if (tight && head_dim % 8) return OC_ERR_INVALID;
+  const int64_t tiles = seq_len / 64;
+  const int64_t groups = (int64_t)num_seqs * num_kv_heads;
+  const size_t base = oc_workspace_bytes(groups, group, tiles, head_dim);
+  if (!workspace || base == 0 || workspace_bytes < base + cached_extra(groups, tiles)) return OC_ERR_WORKSPACE;
+  int* count = reinterpret_cast<int*>(static_cast<char*>(workspace) + base);
+  int* list = reinterpret_cast<int*>(static_cast<char*>(workspace) + base + pad256(4 * (size_t)groups));
+  if (q_dtype != OC_F32 && q_dtype != OC_F16 && q_dtype != OC_BF16) return OC_ERR_UNSUPPORTED;
+  oc::GateArgs a{};
+  a.q = q;
+  a.q_dtype = q_dtype;
+  a.q_seq_stride = q_seq_stride;
+  a.q_head_stride = q_head_stride;
+  a.num_seqs = num_seqs;
+  a.num_kv_heads = num_kv_heads;
+  a.group = group;
+  a.head_dim = head_dim;
+  a.norms = norms;
+  a.norm_seq_stride = norm_seq_stride;
+  a.norm_head_stride = norm_head_stride;
+  a.num_tiles = (int)tiles;
+  a.max_tiles = (int)tiles;
+  a.thr = gate_threshold(tau, head_dim);
+  a.tight = tight;
+  a.low_band = 8;
+  a.stat_median = q_stat;
+  a.evict = evict_out;
+  a.evict_stride = tiles;
+  a.q_norms = q_norms_out;
+  a.list = list;
+  a.list_stride = tiles;
+  a.count = count;
+  const int g = oc::launch_decode_gate(a, static_cast<cudaStream_t>(stream));
+  if (g != OC_OK) return g;
+  DecodeParams p = blank();
+  p.gate = oc::GATE_LIST;
+  p.tile_list = list;
+  p.list_count = count;
+  p.list_stride = tiles;
+  return v3_common(p, q, q_dtype, q_seq_stride, q_head_stride, keys, k_dtype, k_seq_stride, k_head_stride,
+                   k_tok_stride, values, v_dtype, v_seq_stride, v_head_stride, v_tok_stride, num_seqs,
+                   num_kv_heads, group, seq_len, head_dim, 1, num_sms, out, out_dtype, out_seq_stride,
+                   out_head_stride, nullptr, retained, status, workspace, base, stream);
 }
 
 }  // extern "C"

@@ -64,7 +64,10 @@ enum : int { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2, DT_F8E4M3 = 3 };
 //   GATE_ZETA_ATTN: evict iff zeta > thr        (attention loops; NaN retains)
 //   GATE_ZETA_MASK: retain iff zeta <= thr      (mask helper; NaN evicts)
 //   GATE_CS:        evict iff bound <= thr      (V3 Cauchy-Schwarz; NaN retains)
-enum : int { GATE_ZETA_ATTN = 0, GATE_ZETA_MASK = 1, GATE_CS = 2 };
+//   GATE_LIST:      no gate; each (sequence, kv head) decodes the tiles of its
+//                   list (tile_list / list_count), e.g. the tiles a cached-norm
+//                   gate retained, so evicted tiles cost no K or V read at all
+enum : int { GATE_ZETA_ATTN = 0, GATE_ZETA_MASK = 1, GATE_CS = 2, GATE_LIST = 3 };
 enum : int { LAYOUT_LINEAR = 0, LAYOUT_PAGED = 1 };
 enum : uint32_t { ST_TIMEOUT = 1u, ST_BAD_PAGE = 2u, ST_BAD_SEQLEN = 4u };
 
@@ -135,6 +138,10 @@ struct DecodeParams {
   // gate and the logits.  k_deq_dtype < 0: keys are used as stored.
   int k_deq_dtype;
   float k_deq_scale;
+  // GATE_LIST: tiles of (seq, kv head) g are tile_list[g*list_stride + k], k < list_count[g]
+  const int* tile_list;
+  const int* list_count;
+  int64_t list_stride;
 };
 
 // ---------------------------------------------------------------- conversions
@@ -421,6 +428,10 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       if ((L < 0 || (L & 63) || L > p.num_tiles * 64) && blockIdx.x == 0) atomicOr(p.status, ST_BAD_SEQLEN);
       const int lt = L < 0 ? 0 : (L >> 6);
       T = lt < T ? lt : T;
+    }
+    if (p.list_count != nullptr) {
+      const int c = p.list_count[u / nchunks];
+      T = c < 0 ? 0 : (c < T ? c : T);
     }
     tp[u + 1] = T;
   }
@@ -747,6 +758,11 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   int64_t u_end_iss = 0;  // first flattened tile after unit u_iss
   int64_t f_iss = fa;
   SplitIter it_iss;
+  // GATE_LIST: list entry of the next tile to issue, loaded one issue ahead
+  int list_pf = 0;
+  auto list_load = [&](int u, int64_t f) {
+    return p.tile_list[(int64_t)(u / nchunks) * p.list_stride + (f - tp[u])];
+  };
   auto enter_unit = [&](int u, int64_t f) {  // issue cursor enters unit u at flattened tile f
     u_iss = u;
     u_end_iss = tp[u + 1];
@@ -757,6 +773,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       pf_unit = u;
     }
     it_iss.init((int)(f - tp[u]), tp[u + 1] - tp[u], S);
+    if (p.tile_list != nullptr) list_pf = list_load(u, f);
   };
   if (fb > fa) enter_unit(u_first, fa);
   auto issue_next = [&](uint32_t s) {
@@ -766,7 +783,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         while (f_iss >= tp[u + 1]) ++u;
         enter_unit(u, f_iss);
       }
-      const int tile = it_iss.tile();
+      const int tile = p.tile_list != nullptr ? list_pf : it_iss.tile();
       issue(s, seq_iss, kvh_iss, tile, false);
       if (lane == (int)s) {
         dsc_a = 2 * (int)(f_iss - fa);
@@ -774,6 +791,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       }
       it_iss.next();
       ++f_iss;
+      if (p.tile_list != nullptr && f_iss < u_end_iss && f_iss < fb) list_pf = list_load(u_iss, f_iss);
     } else if (lane == (int)s) {
       dsc_a = -1;
     }
@@ -880,7 +898,8 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       }
 
       // ---- band energies
-      float score;
+      float score = 0.f;
+      if (p.gate != GATE_LIST) {
       if constexpr (TC) {
         score = tc_gate(ts);
       } else {
@@ -968,8 +987,10 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
           score = qmax * kn;
         }
       }
+      }
       bool keep;
-      if (p.gate == GATE_ZETA_ATTN) keep = !(score > p.thr);
+      if (p.gate == GATE_LIST) keep = true;
+      else if (p.gate == GATE_ZETA_ATTN) keep = !(score > p.thr);
       else if (p.gate == GATE_ZETA_MASK) keep = (score <= p.thr);
       else keep = !(score <= p.thr);
 

@@ -115,11 +115,25 @@ def case_inputs(name: str) -> dict:
         values = rng.standard_normal(keys.shape, dtype=np.float32)
         q = rng.standard_normal((2, 64), dtype=np.float32)
         return {"q": q, "keys": keys, "values": values, "thresholds": [999.0, 1.0]}
+    if name == "norm_cache":
+        # SpectralNormCache.populate_from_keys, bands [48, 64) (the model path's) and [32, 64)
+        rng = np.random.default_rng(41)
+        keys, _ = tile_mixture(rng, (4,), 12, 64)
+        return {"keys": keys, "thresholds": [48.0, 32.0]}
+    if name == "decode_gate":
+        # _pytorch_decode_gate: 4 kv heads x G 4, head_dim 64, 12 valid of 16 tiles;
+        # half of the query heads high-band-zeroed; thresholds are tau values
+        rng = np.random.default_rng(42)
+        q = rng.standard_normal((16, 64), dtype=np.float32)
+        q[1::2] = np.repeat(q[1::2].reshape(8, 8, 8).mean(-1), 8, axis=-1)  # block-constant: q_high = 0
+        norms = np.abs(rng.standard_normal((4, 16), dtype=np.float32)) * 60.0
+        return {"q": q, "norms": norms, "thresholds": [0.05, 0.1, 0.2]}
     raise KeyError(name)
 
 
 CASES = ["mask_semantic", "mask_random", "mask_mixture_hd64", "v1_config1", "v2_f16",
-         "v2_bf16_hd64", "v3_bf16", "v3_f32_g1", "paged_f32", "v2_fp8"]
+         "v2_bf16_hd64", "v3_bf16", "v3_f32_g1", "paged_f32", "v2_fp8",
+         "norm_cache", "decode_gate"]
 
 
 def fp8_quantize(keys_f32):

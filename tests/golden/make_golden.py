@@ -23,7 +23,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 sys.path.insert(0, HERE)
 
 
-def main(ref_root: str) -> None:
+def main(ref_root: str, only=None) -> None:
     sys.path.insert(0, os.path.join(ref_root, "src"))
     import torch
     from orthocache_gpu.triton_kernels import fwht_fused_prototype as fw
@@ -37,7 +37,7 @@ def main(ref_root: str) -> None:
     torch.set_num_threads(1)
     T = torch.from_numpy
 
-    for name in CASES:
+    for name in (only or CASES):
         inp = case_inputs(name)
         out = {}
         arrays = [v for v in inp.values() if isinstance(v, np.ndarray)]
@@ -94,11 +94,29 @@ def main(ref_root: str) -> None:
             for i, z in enumerate(ths):
                 o, _ = fe.fused_orthocache_attention_v2(q, k8, v, z, k_scale=scale)
                 out[f"out_{i}"] = o.numpy()
+        elif name == "norm_cache":
+            from orthocache_gpu import norm_cache as ncm
+            k = T(inp["keys"])
+            w = fw.generate_walsh_matrix(64)
+            for i, hs in enumerate(ths):
+                c = ncm.SpectralNormCache(4, 16, torch.device("cpu"))
+                c.populate_from_keys(k, w, high_start=int(hs), high_end=64)
+                out[f"norms_{i}"] = c.cache.numpy()
+                out[f"valid_{i}"] = c.valid_tiles.numpy()
+        elif name == "decode_gate":
+            from orthocache_gpu.triton_kernels import decode_gate as dg
+            q, nrm = T(inp["q"]), T(inp["norms"])
+            out["q_high"] = dg.compute_q_high_norm_exact(q).numpy()
+            for i, tau in enumerate(ths):
+                for tight in (True, False):
+                    m, qn = dg._pytorch_decode_gate(q, nrm, tau, 12, 4, 64, tight=tight)
+                    out[f"evict_{i}_{int(tight)}"] = m.numpy()
+                    out[f"qn_{i}_{int(tight)}"] = qn.numpy()
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
         print("wrote", name)
 
 
 if __name__ == "__main__":
-    if len(sys.argv) != 2:
-        sys.exit("usage: make_golden.py <reference project root>")
-    main(sys.argv[1])
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference project root> [case ...]")
+    main(sys.argv[1], sys.argv[2:] or None)

@@ -119,3 +119,30 @@ def test_lse_merge_equals_unsplit():
     # all splits empty -> zeros
     np.testing.assert_array_equal(orc.lse_merge(np.full(3, -1e9), np.zeros(3), np.zeros((3, hd))),
                                   np.zeros(hd))
+
+
+def test_norm_cache_matches_reference():
+    inp, z = load("norm_cache")
+    for i, hs in enumerate(z["thresholds"]):
+        norms = orc.tile_high_norms(inp["keys"], int(hs), 64)
+        ref = z[f"norms_{i}"]
+        np.testing.assert_allclose(norms, ref[:, :12], rtol=2e-6, atol=0)
+        assert not ref[:, 12:].any() and (z[f"valid_{i}"] == 12).all()
+
+
+# |q_high| = sqrt(|q|^2 - |q_low|^2) cancels for queries without high band:
+# float32 summation order alone leaves sqrt(~1e-7 * |q|^2) ~ 3e-3 absolute there
+QH_ATOL = 4e-3
+
+
+def test_decode_gate_matches_reference():
+    inp, z = load("decode_gate")
+    np.testing.assert_allclose(orc.q_high_norm(inp["q"]), z["q_high"], rtol=1e-5, atol=QH_ATOL)
+    for i, tau in enumerate(z["thresholds"]):
+        for tight in (True, False):
+            evict, s, bound = orc.decode_gate(inp["q"], inp["norms"], tau, 12, 4, tight=tight)
+            np.testing.assert_allclose(s, z[f"qn_{i}_{int(tight)}"], rtol=1e-5, atol=QH_ATOL)
+            ref = z[f"evict_{i}_{int(tight)}"]
+            near = orc.near_threshold(bound, tau * 64 * 64)
+            assert np.array_equal(evict[~near], ref[~near]), (tau, tight)
+            assert not ref[:, 12:].any()
