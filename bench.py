@@ -129,22 +129,29 @@ def algorithmic_bytes(num_tiles_total, retained, esz=2, hd=HEAD_DIM, heads=HEADS
 
 
 def dense_decode_us(q, k, v, reps=50):
-    """Dense flash-decoding on the same inputs (flashinfer if usable, else torch SDPA)."""
+    """Dense decode of all K and V on the same inputs: flashinfer and torch SDPA.
+
+    Timed like ours (``us_graph``: a CUDA graph of 50 calls; ``us_eager``:
+    back-to-back eager calls), so the comparison is like for like.
+    """
     res = {}
+    arms = {}
     try:
         import flashinfer
-        fn = lambda: flashinfer.single_decode_with_kv_cache(q, k, v, kv_layout="HND")  # noqa: E731
-        fn()
-        res["flashinfer_us"] = time_fn(fn, reps)
+        arms["flashinfer"] = lambda: flashinfer.single_decode_with_kv_cache(q, k, v, kv_layout="HND")  # noqa: E731
+        arms["flashinfer"]()
     except Exception as e:  # noqa: BLE001
+        arms.pop("flashinfer", None)
         res["flashinfer_error"] = type(e).__name__
-    try:
-        qq, kk, vv = q[None, :, None, :], k[None], v[None]
-        fn = lambda: torch.nn.functional.scaled_dot_product_attention(qq, kk, vv)  # noqa: E731
-        fn()
-        res["torch_sdpa_us"] = time_fn(fn, reps)
-    except Exception as e:  # noqa: BLE001
-        res["torch_sdpa_error"] = type(e).__name__
+    qq, kk, vv = q[None, :, None, :], k[None], v[None]
+    arms["torch_sdpa"] = lambda: torch.nn.functional.scaled_dot_product_attention(qq, kk, vv)  # noqa: E731
+    for name, fn in arms.items():
+        try:
+            res[f"{name}_us_eager"] = time_fn(fn, reps)
+            g = graph_of(lambda i=0, f=fn: f(), 50)
+            res[f"{name}_us_graph"] = time_fn(g.replay, 10) / 50
+        except Exception as e:  # noqa: BLE001
+            res[f"{name}_error"] = type(e).__name__
     return res
 
 
@@ -202,81 +209,194 @@ def _graph_us(fn, n=20, reps=5):
     return time_fn(g.replay, reps) / n
 
 
-def extra_configs(dev):
-    """The reference's other measured configurations, timed on one GPU (graph-replayed).
+def _time_max(fn, dist, n=20, reps=5, graph=True):
+    """µs per call of fn on this rank (graph-replayed unless graph=False), max over ranks."""
+    if graph:
+        g = graph_of(lambda i=0: fn(), n)
+        run, calls = g.replay, n
+    else:
+        run, calls = fn, 1
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_.record()
+    for _ in range(reps):
+        run()
+    e_.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([s_.elapsed_time(e_) * 1000.0 / (reps * calls)], device="cuda")
+    if dist:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
 
-    Config 3: V3 Cauchy-Schwarz GQA, batch 16, 32 query / 8 kv heads, hd 128,
-    32K tokens, bf16, half of the query heads with their high band zeroed,
-    tau 150 (about half the tiles evicted).  Config 4: paged GQA, 64
-    sequences of U[2K, 64K] tokens (multiples of 64), 16-token pages in a
-    permuted pool, 32 / 8 heads, hd 128, fp16, Cauchy-Schwarz gate tau 150.
-    Bytes = all K tiles + retained V tiles (+ q, out).  Inputs are larger than L2.
+
+def _sum_ranks(x, dist):
+    t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+    if dist:
+        torch.distributed.all_reduce(t)
+    return float(t.item())
+
+
+def _line(name, us, nbytes, evict, peak, extra=None):
+    gbs = nbytes / (us * 1e-6) / 1e9
+    d = {"config": name, "us": round(us, 2), "gbs": round(gbs, 1), "frac_of_measured_peak_per_gpu": None,
+         "evict": round(evict, 3), "algorithmic_bytes": int(nbytes)}
+    d.update(extra or {})
+    return d
+
+
+def lpt_partition(lengths, world):
+    """Sequences of ``lengths`` assigned to ``world`` ranks, longest first to the least-loaded rank."""
+    load, parts = [0] * world, [[] for _ in range(world)]
+    for i in sorted(range(len(lengths)), key=lambda j: -int(lengths[j])):
+        r = min(range(world), key=lambda w: load[w])
+        parts[r].append(i)
+        load[r] += int(lengths[i])
+    return [sorted(p) for p in parts]
+
+
+def extra_configs(dev, rank, world, dist, peak):
+    """The reference's other measured configurations, partitioned over the ranks.
+
+    Every configuration is ONE fixed workload split across the N GPUs (strong
+    scaling); time = max over ranks of the graph-replayed per-call time;
+    GB/s = all ranks' algorithmic bytes (all K tiles + retained V tiles) / time.
+
+    * config 3: V3 Cauchy-Schwarz GQA, batch 16, 32 query / 8 kv heads, hd
+      128, 32K tokens, bf16, half of the query heads high-band-zeroed, tau 150;
+      the 16 sequences are split over the ranks (batch partitioning).
+    * cached gate: the same shapes decoded with the O(1) gate from a
+      spectral norm cache (band [48, 64), tau at the median bound): evicted
+      tiles cost no K or V read; bytes = retained K + retained V + norms.
+    * config 4: paged GQA, 64 sequences of U[2K, 64K] tokens, 16-token pages
+      in a permuted pool, 32 / 8 heads, hd 128, fp16, tau 150; sequences are
+      assigned to ranks longest first to the least-loaded rank (balanced by
+      the sum of lengths), each rank holding only its pages.
+    * config 5a: one 512K-token sequence, 8 kv heads, G 8, bf16, tau 150,
+      split into N tile-aligned shards; a step is the shard decode + NCCL
+      all-gather of the (m, l, acc) states + the log-sum-exp merge (eager, as
+      a serving loop would run it); the all-gather alone is reported too.
+    * config 5b (N = 1 only): the TinyLlama-shaped model.
     """
     import orthocache_gpu_b200 as oc
+    from orthocache_gpu_b200 import distributed as ocd
     out = []
     g = torch.Generator(device=dev)
-    g.manual_seed(3)
+    g.manual_seed(3 + 1000 * rank)
+
+    # ---- config 3 and the cached-gate decode of the same shapes
     B, KVH, G, S, HD, TAU = 16, 8, 4, 32768, 128, 150.0
-    k = _mixture_device((B, KVH), S, HD, g, dev).to(torch.bfloat16)
+    my = list(range(rank * B // world, (rank + 1) * B // world))
+    nb_ = len(my)
+    k = _mixture_device((nb_, KVH), S, HD, g, dev).to(torch.bfloat16)
     v = torch.randn(k.shape, generator=g, device=dev).to(torch.bfloat16)
-    q = _zero_high_half(torch.randn((B, KVH * G, HD), generator=g, device=dev)).to(torch.bfloat16)
+    q = _zero_high_half(torch.randn((nb_, KVH * G, HD), generator=g, device=dev)).to(torch.bfloat16)
     kept = oc.fused_orthocache_attention_v3_gqa(q, k, v, TAU, G)[1]["tiles_retained"]
-    us = _graph_us(lambda: oc.fused_orthocache_attention_v3_gqa(q, k, v, TAU, G, stats=False))
-    nt = B * KVH * (S // 64)
-    nb = nt * 64 * HD * 2 + kept * 64 * HD * 2
-    out.append({"config": "V3 GQA batch 16, 32Q/8KV, hd 128, 32K, bf16, tau 150", "us": round(us, 2),
-                "gbs": round(nb / (us * 1e-6) / 1e9, 1), "evict": round(1 - kept / nt, 3),
-                "algorithmic_bytes": int(nb)})
-    del k, v, q
+    us = _time_max(lambda: oc.fused_orthocache_attention_v3_gqa(q, k, v, TAU, G, stats=False), dist)
+    nt = nb_ * KVH * (S // 64)
+    nbytes = _sum_ranks(nt * 64 * HD * 2 + kept * 64 * HD * 2, dist)
+    ntot = _sum_ranks(nt, dist)
+    keptt = _sum_ranks(kept, dist)
+    out.append(_line(f"V3 GQA batch 16 split over {world} GPU(s), 32Q/8KV, hd 128, 32K, bf16, tau 150", us, nbytes,
+                     1 - keptt / ntot, peak, {"n_gpus": world, "scaling": "strong"}))
+    norms = oc.tile_high_norms(k.reshape(nb_ * KVH, S, HD)).reshape(nb_, KVH, S // 64)
+    qn = oc.compute_q_high_norm_exact(q).reshape(nb_, KVH, G).amax(-1)
+    tau_c = float((qn[..., None] * norms).median()) / (64 * HD)
+    tau_c = float(_sum_ranks(tau_c, dist) / world)
+    kept = oc.fused_orthocache_attention_cached(q, k, v, norms, tau_c, G)[1]["tiles_retained"]
+    us = _time_max(lambda: oc.fused_orthocache_attention_cached(q, k, v, norms, tau_c, G, stats=False), dist)
+    nbytes = _sum_ranks(2 * kept * 64 * HD * 2 + norms.numel() * 4, dist)
+    keptt = _sum_ranks(kept, dist)
+    out.append(_line(f"cached-norm gate decode, V3 shapes (batch 16 split over {world} GPU(s)), tau at the "
+                     "median bound", us, nbytes, 1 - keptt / ntot, peak,
+                     {"n_gpus": world, "scaling": "strong", "bytes": "retained K + retained V + norms"}))
+    del k, v, q, norms
     torch.cuda.empty_cache()
 
+    # ---- config 4: paged, balanced by the sum of lengths
     rng = np.random.default_rng(0)
     NS, BS = 64, 16
-    lens = rng.integers(2048, 65536 + 1, size=NS)
-    lens = (lens - lens % 64).astype(np.int64)
+    lens_all = rng.integers(2048, 65536 + 1, size=NS)
+    lens_all = (lens_all - lens_all % 64).astype(np.int64)
+    mine = lpt_partition(lens_all, world)[rank]
+    lens = lens_all[mine]
     nblk = lens // BS
     total = int(nblk.sum())
-    perm = torch.from_numpy(rng.permutation(total).astype(np.int64)).to(dev)
+    perm = torch.from_numpy(np.random.default_rng(1 + rank).permutation(total).astype(np.int64)).to(dev)
     kc = torch.empty((total, KVH, BS, HD), dtype=torch.float16, device=dev)
     vc = torch.empty_like(kc)
-    tables = torch.zeros((NS, int(nblk.max())), dtype=torch.int32, device=dev)
+    tables = torch.zeros((len(mine), int(nblk.max())), dtype=torch.int32, device=dev)
     pos = 0
-    for s_ in range(NS):
-        L, nb_ = int(lens[s_]), int(nblk[s_])
-        pages = perm[pos:pos + nb_]
-        pos += nb_
+    for i in range(len(mine)):
+        L, nbk = int(lens[i]), int(nblk[i])
+        pages = perm[pos:pos + nbk]
+        pos += nbk
         ks = _mixture_device((KVH,), L, HD, g, dev)
-        kc[pages] = ks.reshape(KVH, nb_, BS, HD).permute(1, 0, 2, 3).to(torch.float16)
-        vc[pages] = torch.randn((nb_, KVH, BS, HD), generator=g, device=dev).to(torch.float16)
-        tables[s_, :nb_] = pages.to(torch.int32)
-        tables[s_, nb_:] = pages[0].to(torch.int32)
+        kc[pages] = ks.reshape(KVH, nbk, BS, HD).permute(1, 0, 2, 3).to(torch.float16)
+        vc[pages] = torch.randn((nbk, KVH, BS, HD), generator=g, device=dev).to(torch.float16)
+        tables[i, :nbk] = pages.to(torch.int32)
+        tables[i, nbk:] = pages[0].to(torch.int32)
         del ks
     seq_lens = torch.from_numpy(lens.astype(np.int32)).to(dev)
-    qp = _zero_high_half(torch.randn((NS, KVH * G, HD), generator=g, device=dev)).to(torch.float16)
+    qp = _zero_high_half(torch.randn((len(mine), KVH * G, HD), generator=g, device=dev)).to(torch.float16)
     kw = dict(tau=TAU, seq_lens=seq_lens)
     kept = oc.fused_orthocache_attention_paged(qp, kc, vc, tables, None, **kw)[1]["tiles_retained"]
-    us = _graph_us(lambda: oc.fused_orthocache_attention_paged(qp, kc, vc, tables, None, stats=False, **kw))
+    us = _time_max(lambda: oc.fused_orthocache_attention_paged(qp, kc, vc, tables, None, stats=False, **kw), dist)
     nt = int((lens // 64).sum()) * KVH
-    nb = nt * 64 * HD * 2 + kept * 64 * HD * 2
-    out.append({"config": "paged GQA, 64 seqs U[2K,64K], page 16, 32Q/8KV, hd 128, fp16, tau 150",
-                "us": round(us, 2), "gbs": round(nb / (us * 1e-6) / 1e9, 1), "evict": round(1 - kept / nt, 3),
-                "algorithmic_bytes": int(nb)})
-    del kc, vc, qp
+    nbytes = _sum_ranks(nt * 64 * HD * 2 + kept * 64 * HD * 2, dist)
+    out.append(_line(f"paged GQA, 64 seqs U[2K,64K] balanced over {world} GPU(s), page 16, 32Q/8KV, hd 128, "
+                     "fp16, tau 150", us, nbytes, 1 - _sum_ranks(kept, dist) / _sum_ranks(nt, dist), peak,
+                     {"n_gpus": world, "scaling": "strong",
+                      "tokens_per_rank_max_over_mean": round(
+                          max(sum(int(lens_all[j]) for j in p) for p in lpt_partition(lens_all, world)) /
+                          (lens_all.sum() / world), 4)}))
+    del kc, vc, qp, tables
     torch.cuda.empty_cache()
 
-    # config 5b: TinyLlama-1.1B-shaped random-init model, 16K random-token prompt,
-    # 256 greedy steps, fused gate in every layer (median-calibrated tau) vs dense SDPA
-    from orthocache_gpu_b200.model import GatedLlama, LlamaShape
-    m = GatedLlama(LlamaShape(), max_len=16384 + 320, device=dev, seed=5)
-    prompt = torch.randint(0, 32000, (16384,), generator=g, device=dev)
-    row = {"config": "TinyLlama-1.1B-shaped random-init, 22 layers, 32Q/4KV, hd 64, bf16, 16K prompt, "
-                     "256 greedy steps (eager per-step device time, median)"}
-    for mode, key in (("median", "fused_ms_per_token"), (None, "dense_sdpa_ms_per_token")):
-        r = m.generate(prompt, 256, tau_mode=mode)
-        row[key] = round(r["ms_per_token"], 3)
-    out.append(row)
-    del m
+    # ---- config 5a: one 512K sequence, sequence-sharded
+    S5, G5 = 512 * 1024, 8
+    a_, b_ = ocd.shard_range(S5, world, rank)
+    k = _mixture_device((KVH,), b_ - a_, HD, g, dev).to(torch.bfloat16)
+    v = torch.randn(k.shape, generator=g, device=dev).to(torch.bfloat16)
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(55)  # the same query on every rank
+    q = _zero_high_half(torch.randn((KVH * G5, HD), generator=gq, device=dev)).to(torch.bfloat16)
+    kept = ocd.shard_partials(q, k, v, TAU, G5)[3]
+    nt = KVH * (b_ - a_) // 64
+    nbytes = _sum_ranks(nt * 64 * HD * 2 + kept * 64 * HD * 2, dist)
+    extra = {"n_gpus": world, "scaling": "strong"}
+    if dist:
+        us = _time_max(lambda: ocd.sequence_sharded_decode(q, k, v, TAU, G5), dist, graph=False, reps=50)
+        st = ocd.pack_state(*ocd.shard_partials(q, k, v, TAU, G5, stats=False)[:3])
+        extra["all_gather_us"] = round(_time_max(lambda: ocd.gather_states(st), dist, graph=False, reps=50), 2)
+        extra["shard_decode_us"] = round(_time_max(
+            lambda: ocd.shard_partials(q, k, v, TAU, G5, stats=False), dist), 2)
+    else:
+        us = _time_max(lambda: oc.fused_orthocache_attention_v3_gqa(q, k, v, TAU, G5, stats=False), dist)
+    out.append(_line(f"512K-token sequence, 8 KV heads, G 8, bf16, tau 150, {world} shard(s) + all-gather + merge",
+                     us, nbytes, 1 - _sum_ranks(kept, dist) / _sum_ranks(nt, dist), peak, extra))
+    del k, v
     torch.cuda.empty_cache()
+    for d in out:
+        d["frac_of_measured_peak_per_gpu"] = round(d["gbs"] / world / peak, 4)
+
+    # ---- config 5b: TinyLlama-1.1B-shaped random-init model (one GPU)
+    if world == 1:
+        from orthocache_gpu_b200.model import GatedLlama, LlamaShape
+        m = GatedLlama(LlamaShape(), max_len=16384 + 320, device=dev, seed=5)
+        prompt = torch.randint(0, 32000, (16384,), generator=g, device=dev)
+        row = {"config": "TinyLlama-1.1B-shaped random-init, 22 layers, 32Q/4KV, hd 64, bf16, 16K prompt, "
+                         "256 greedy steps (eager per-step device time, median)",
+               "weight_read_bound_ms": round(m.weight_bytes() / (peak * 1e9) * 1e3, 3)}
+        for mode, key in (("median", "fused_ms_per_token"), ("flash", "dense_flashinfer_ms_per_token")):
+            r = m.generate(prompt, 256, tau_mode=mode)
+            row[key] = round(r["ms_per_token"], 3)
+        out.append(row)
+        del m
+        torch.cuda.empty_cache()
     return out
 
 
@@ -320,7 +440,7 @@ def main():
     if dist:
         torch.cuda.set_device(local)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local),
-                                             timeout=datetime.timedelta(seconds=120))
+                                             timeout=datetime.timedelta(seconds=600))
     dev = torch.device("cuda", local)
     seq = a.seq
     ntiles = HEADS * (seq // 64)
@@ -394,9 +514,9 @@ def main():
     value = per_step_bytes * steps * world / (ms_max / 1e3) / 1e9
     launch_us = ms / steps * 1000.0
     achieved = per_step_bytes / (launch_us * 1e-6) / 1e9
-    peak, peak_kind = measured_peaks()
 
     if a.quick:
+        peak, _ = measured_peaks()
         if rank == 0:
             print(json.dumps({"metric": metric, "value": round(value, 1), "unit": "GB/s", "steps": steps,
                               "launch_us": round(launch_us, 3), "achieved": round(achieved, 1)}))
@@ -430,6 +550,7 @@ def main():
     e2e_value = bytes_per[0] * a.e2e_steps * world / (float(te.item()) / 1e3) / 1e9
 
     extra = {}
+    peak, peak_kind = measured_peaks()
     if rank == 0 and not a.no_sweep:
         sweep = []
         for sl in (1024, 2048, 4096, 8192, 16384, 32768):
@@ -450,7 +571,10 @@ def main():
             if sl != seq:
                 del qs, ks, vs
         extra["sweep"] = sweep
-        extra["configs"] = extra_configs(dev)
+    if not a.no_sweep:
+        cfgs = extra_configs(dev, rank, world, dist, peak)
+        if rank == 0:
+            extra["configs"] = cfgs
 
     if rank == 0:
         cb = cpu_baseline(seq, a.cpu_sample_heads or 8)

@@ -215,7 +215,11 @@ size_t oc_cached_workspace_bytes(int64_t num_groups, int group, int64_t num_tile
  * with element strides.  evict_out (nullable, (num_seqs, num_kv_heads,
  * seq_len/64)): the gate's evict flags.  The reference evaluates this gate
  * and masks the logits of the dense product (perplexity_eval.py:554-674);
- * the output is the same softmax over the retained tiles. */
+ * the output is the same softmax over the retained tiles.  With m_out, l_out
+ * and acc_out (all or none; (num_seqs*num_kv_heads*group) and that x
+ * head_dim floats) the merged softmax state of each query head is written
+ * instead of out (as oc_fused_attention_v3_shard), e.g. to merge with a
+ * ragged tail of tokens through oc_lse_merge. */
 int oc_fused_attention_cached(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
                               const void* keys, int k_dtype, int64_t k_seq_stride, int64_t k_head_stride,
                               int64_t k_tok_stride, const void* values, int v_dtype, int64_t v_seq_stride,
@@ -223,9 +227,9 @@ int oc_fused_attention_cached(const void* q, int q_dtype, int64_t q_seq_stride, 
                               int group, int64_t seq_len, int head_dim, const float* norms,
                               int64_t norm_seq_stride, int64_t norm_head_stride, double tau, int tight,
                               int q_stat, int num_sms, void* out, int out_dtype, int64_t out_seq_stride,
-                              int64_t out_head_stride, uint8_t* evict_out, float* q_norms_out,
-                              uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
-                              void* stream);
+                              int64_t out_head_stride, float* m_out, float* l_out, float* acc_out,
+                              uint8_t* evict_out, float* q_norms_out, uint32_t* retained, uint32_t* status,
+                              void* workspace, size_t workspace_bytes, void* stream);
 
 /* Allocation-free variant of oc_fused_attention_v2 (no counterpart in the
  * reference).  For callers that cannot allocate device memory: code running

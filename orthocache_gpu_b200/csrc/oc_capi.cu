@@ -351,6 +351,12 @@ static int v3_common(DecodeParams& p, const void* q, int q_dtype, int64_t q_seq_
       if (p.seq_lens) pc.seq_lens = p.seq_lens + s0;
     }
     if (out) pc.out = static_cast<char*>(out) + s0 * out_seq_stride * osz;
+    if (p.sh_acc) {  // merged states are indexed by (sequence, query head) inside a launch
+      const int64_t u0 = s0 * num_kv_heads * group;
+      pc.sh_m = p.sh_m + u0;
+      pc.sh_l = p.sh_l + u0;
+      pc.sh_acc = p.sh_acc + u0 * out_head_stride;
+    }
     if (p.mask) pc.mask = p.mask + s0 * num_kv_heads * tiles;
     pc.stats_add = s0 > 0 ? 1 : 0;  // the first launch sets the count, later ones add
     if (p.tile_list) {
@@ -541,9 +547,10 @@ int oc_fused_attention_cached(const void* q, int q_dtype, int64_t q_seq_stride, 
                               int group, int64_t seq_len, int head_dim, const float* norms,
                               int64_t norm_seq_stride, int64_t norm_head_stride, double tau, int tight,
                               int q_stat, int num_sms, void* out, int out_dtype, int64_t out_seq_stride,
-                              int64_t out_head_stride, uint8_t* evict_out, float* q_norms_out,
-                              uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
-                              void* stream) {
+                              int64_t out_head_stride, float* m_out, float* l_out, float* acc_out,
+                              uint8_t* evict_out, float* q_norms_out, uint32_t* retained, uint32_t* status,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  if ((acc_out != nullptr) != (m_out != nullptr) || (acc_out != nullptr) != (l_out != nullptr)) return OC_ERR_INVALID;
   if (!norms || num_seqs < 1 || num_kv_heads < 1 || group < 1 || group > 64 || seq_len < 0 || (seq_len % 64))
     return OC_ERR_INVALID;
   if (tight && head_dim % 8) return OC_ERR_INVALID;
@@ -585,6 +592,15 @@ int oc_fused_attention_cached(const void* q, int q_dtype, int64_t q_seq_stride, 
   p.tile_list = list;
   p.list_count = count;
   p.list_stride = tiles;
+  if (acc_out) {  // merged softmax states (m in log2 units, l, unnormalised acc) instead of the output
+    p.sh_m = m_out;
+    p.sh_l = l_out;
+    p.sh_acc = acc_out;
+    return v3_common(p, q, q_dtype, q_seq_stride, q_head_stride, keys, k_dtype, k_seq_stride, k_head_stride,
+                     k_tok_stride, values, v_dtype, v_seq_stride, v_head_stride, v_tok_stride, num_seqs,
+                     num_kv_heads, group, seq_len, head_dim, 1, num_sms, nullptr, OC_F32, 0, head_dim, nullptr,
+                     retained, status, workspace, base, stream);
+  }
   return v3_common(p, q, q_dtype, q_seq_stride, q_head_stride, keys, k_dtype, k_seq_stride, k_head_stride,
                    k_tok_stride, values, v_dtype, v_seq_stride, v_head_stride, v_tok_stride, num_seqs,
                    num_kv_heads, group, seq_len, head_dim, 1, num_sms, out, out_dtype, out_seq_stride,

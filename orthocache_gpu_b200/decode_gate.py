@@ -102,6 +102,62 @@ def apply_decode_mask_vectorized(logits: torch.Tensor, mask: torch.Tensor, G: in
 apply_decode_mask = apply_decode_mask_vectorized  # same result as the reference's looped form (:309-342)
 
 
+def _cached_call(q, keys, values, norm_cache, tau, G, tight, q_stat, return_mask, stats, states):
+    batched = keys.ndim == 4
+    num_kv_heads, seq_len, head_dim = keys.shape[-3:]
+    num_tiles = seq_len // TILE_SIZE
+    assert seq_len == num_tiles * TILE_SIZE, f"seq_len {seq_len} not divisible by tile_size {TILE_SIZE}"
+    assert q.shape[-2] == num_kv_heads * G, (
+        f"num_query_heads ({q.shape[-2]}) != num_kv_heads ({num_kv_heads}) × G ({G})")
+    nc = _norm_tensor(norm_cache)
+    if not batched:
+        q, keys, values, nc = q.unsqueeze(0), keys.unsqueeze(0), values.unsqueeze(0), nc.unsqueeze(0)
+    num_seqs = keys.shape[0]
+    assert nc.shape[-2] >= num_kv_heads and nc.shape[-1] >= num_tiles and nc.shape[0] == num_seqs
+    input_dtype = q.dtype
+    dev = _lib.require_cuda(q, keys, values, nc)
+    nc = nc if (nc.dtype == torch.float32 and nc.stride(-1) == 1) else nc.float().contiguous()
+    q = q if q.stride(-1) == 1 else q.contiguous()
+    keys, values = _lib.harmonize_kv(keys, values)
+    keys, values = _lib.prepare_kv(keys), _lib.prepare_kv(values)
+    hq = num_kv_heads * G
+    if states:
+        m = torch.empty((num_seqs, hq), dtype=torch.float32, device=dev)
+        l = torch.empty_like(m)
+        acc = torch.empty((num_seqs, hq, head_dim), dtype=torch.float32, device=dev)
+        out, optr, st = None, 0, (m.data_ptr(), l.data_ptr(), acc.data_ptr())
+    else:
+        out = torch.empty((num_seqs, hq, head_dim), dtype=input_dtype, device=dev)
+        optr, st = out.data_ptr(), (0, 0, 0)
+    mask = torch.empty((num_seqs, num_kv_heads, num_tiles), dtype=torch.bool, device=dev) if return_mask else None
+    q_norms = torch.empty((num_seqs, num_kv_heads), dtype=torch.float32, device=dev) if return_mask else None
+    stream = _lib.stream_ptr(dev)
+    ws = _lib.workspace(dev, stream)
+    wptr, wbytes = ws.get(_lib.load().oc_cached_workspace_bytes(num_seqs * num_kv_heads, G, num_tiles, head_dim))
+    _lib.check(_lib.load().oc_fused_attention_cached(
+        q.data_ptr(), _lib.dtype_code(q), q.stride(0), q.stride(1),
+        keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1), keys.stride(2),
+        values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1), values.stride(2),
+        num_seqs, num_kv_heads, G, seq_len, head_dim, nc.data_ptr(), nc.stride(0), nc.stride(1),
+        float(tau), int(tight), _Q_STAT[q_stat], _lib.num_sms(dev),
+        optr, _lib.dtype_code(q), hq * head_dim, head_dim, *st,
+        _lib.ptr(mask), _lib.ptr(q_norms), ws.retained_ptr if stats else 0, ws.status_ptr,
+        wptr, wbytes, stream), "fused_orthocache_attention_cached")
+    res = (m, l, acc) if states else (out,)
+    if not batched:
+        res = tuple(t[0] for t in res)
+        if mask is not None:
+            mask, q_norms = mask[0], q_norms[0]
+    meta: Dict[str, Any] = {"num_tiles": num_tiles, "num_kv_heads": num_kv_heads, "num_query_groups": G,
+                            "gate_type": "cached_norm", "tight": tight, "q_stat": q_stat}
+    if batched:
+        meta["num_seqs"] = num_seqs
+    if return_mask:
+        meta["evict_mask"] = mask
+        meta["q_norms"] = q_norms
+    return res, _finish_meta(meta, ws, num_tiles * num_kv_heads * num_seqs, stats)
+
+
 def fused_orthocache_attention_cached(
     q: torch.Tensor,
     keys: torch.Tensor,
@@ -123,48 +179,17 @@ def fused_orthocache_attention_cached(
     Returns (out like q in q's dtype, metadata); ``meta['evict_mask']``
     (with ``return_mask``) is the gate's mask, True = evicted.
     """
-    batched = keys.ndim == 4
-    num_kv_heads, seq_len, head_dim = keys.shape[-3:]
-    G = num_query_groups
-    num_tiles = seq_len // TILE_SIZE
-    assert seq_len == num_tiles * TILE_SIZE, f"seq_len {seq_len} not divisible by tile_size {TILE_SIZE}"
-    assert q.shape[-2] == num_kv_heads * G, (
-        f"num_query_heads ({q.shape[-2]}) != num_kv_heads ({num_kv_heads}) × G ({G})")
-    nc = _norm_tensor(norm_cache)
-    if not batched:
-        q, keys, values, nc = q.unsqueeze(0), keys.unsqueeze(0), values.unsqueeze(0), nc.unsqueeze(0)
-    num_seqs = keys.shape[0]
-    assert nc.shape[-2] >= num_kv_heads and nc.shape[-1] >= num_tiles and nc.shape[0] == num_seqs
-    input_dtype = q.dtype
-    dev = _lib.require_cuda(q, keys, values, nc)
-    nc = nc if (nc.dtype == torch.float32 and nc.stride(-1) == 1) else nc.float().contiguous()
-    q = q if q.stride(-1) == 1 else q.contiguous()
-    keys, values = _lib.harmonize_kv(keys, values)
-    keys, values = _lib.prepare_kv(keys), _lib.prepare_kv(values)
-    out = torch.empty((num_seqs, num_kv_heads * G, head_dim), dtype=input_dtype, device=dev)
-    mask = torch.empty((num_seqs, num_kv_heads, num_tiles), dtype=torch.bool, device=dev) if return_mask else None
-    q_norms = torch.empty((num_seqs, num_kv_heads), dtype=torch.float32, device=dev) if return_mask else None
-    stream = _lib.stream_ptr(dev)
-    ws = _lib.workspace(dev, stream)
-    wptr, wbytes = ws.get(_lib.load().oc_cached_workspace_bytes(num_seqs * num_kv_heads, G, num_tiles, head_dim))
-    _lib.check(_lib.load().oc_fused_attention_cached(
-        q.data_ptr(), _lib.dtype_code(q), q.stride(0), q.stride(1),
-        keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1), keys.stride(2),
-        values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1), values.stride(2),
-        num_seqs, num_kv_heads, G, seq_len, head_dim, nc.data_ptr(), nc.stride(0), nc.stride(1),
-        float(tau), int(tight), _Q_STAT[q_stat], _lib.num_sms(dev),
-        out.data_ptr(), _lib.dtype_code(out), out.stride(0), out.stride(1),
-        _lib.ptr(mask), _lib.ptr(q_norms), ws.retained_ptr if stats else 0, ws.status_ptr,
-        wptr, wbytes, stream), "fused_orthocache_attention_cached")
-    if not batched:
-        out = out[0]
-        if mask is not None:
-            mask, q_norms = mask[0], q_norms[0]
-    meta: Dict[str, Any] = {"num_tiles": num_tiles, "num_kv_heads": num_kv_heads, "num_query_groups": G,
-                            "gate_type": "cached_norm", "tight": tight, "q_stat": q_stat}
-    if batched:
-        meta["num_seqs"] = num_seqs
-    if return_mask:
-        meta["evict_mask"] = mask
-        meta["q_norms"] = q_norms
-    return out, _finish_meta(meta, ws, num_tiles * num_kv_heads * num_seqs, stats)
+    (out,), meta = _cached_call(q, keys, values, norm_cache, tau, num_query_groups, tight, q_stat, return_mask,
+                                stats, False)
+    return out, meta
+
+
+def cached_partials(q, keys, values, norm_cache, tau: float, num_query_groups: int, *, tight: bool = True,
+                    q_stat: str = "max", stats: bool = False):
+    """Like ``fused_orthocache_attention_cached`` but returns each query head's merged softmax state.
+
+    Returns ((m, l, acc), meta): float32 m, l (..., Hq) with m in log2 units
+    and acc (..., Hq, hd) unnormalised, for a log-sum-exp merge with other
+    partial states (a ragged tail of tokens, other sequence shards).
+    """
+    return _cached_call(q, keys, values, norm_cache, tau, num_query_groups, tight, q_stat, False, stats, True)

@@ -62,7 +62,8 @@ class GatedLlama:
     ``tau``: a float (the Cauchy-Schwarz threshold of every layer), or
     "median" to calibrate each layer's threshold at the first decode step as
     the median per-tile bound max_g |q_g| |K_high|_F (about half the tiles
-    evicted), or None for dense decode attention (the reference point).
+    evicted), None for dense decode attention with torch SDPA, or "flash"
+    for dense flash-decoding (flashinfer) of every cached token.
     """
 
     def __init__(self, shape: LlamaShape, max_len: int, device="cuda", dtype=torch.bfloat16, seed: int = 0):
@@ -90,6 +91,11 @@ class GatedLlama:
         self.tau: List[Optional[float]] = [None] * s.layers
         self.kept = 0
         self.tiles = 0
+
+    def weight_bytes(self) -> int:
+        """Bytes of the weights one decode step reads (all layers, final norm, LM head; not the embedding)."""
+        n = sum(t.numel() * t.element_size() for L in self.layers for t in L.values())
+        return n + self.norm.numel() * self.norm.element_size() + self.lm_head.numel() * self.lm_head.element_size()
 
     # ---------------------------------------------------------------- blocks
     def _qkv(self, L, h, pos):
@@ -139,6 +145,9 @@ class GatedLlama:
         full = n - n % 64
         kc, vc = self.k_cache[i], self.v_cache[i]
         scale = LOG2E / math.sqrt(s.head_dim)
+        if tau_mode == "flash":  # dense flash-decoding of every cached token (the fair dense arm)
+            import flashinfer
+            return flashinfer.single_decode_with_kv_cache(q, kc[:, :n], vc[:, :n], kv_layout="HND")
         if tau_mode is None or full == 0:  # dense (reference point, or no whole tile yet)
             a = F.scaled_dot_product_attention(q[None, :, None], kc[None, :, :n], vc[None, :, :n], enable_gqa=True)
             return a[0, :, 0]

@@ -128,12 +128,22 @@ def case_inputs(name: str) -> dict:
         q[1::2] = np.repeat(q[1::2].reshape(8, 8, 8).mean(-1), 8, axis=-1)  # block-constant: q_high = 0
         norms = np.abs(rng.standard_normal((4, 16), dtype=np.float32)) * 60.0
         return {"q": q, "norms": norms, "thresholds": [0.05, 0.1, 0.2]}
+    if name == "hf_hook":
+        # the harness's OrthoCache_GQA_Attention: prefill of 200 tokens, then
+        # decode steps at 201, 255, 256 and 257 cached tokens (tile 3 completes at 256)
+        rng = np.random.default_rng(43)
+        keys, _ = tile_mixture(rng, (2, 2), 5, 64)                      # (B, KVH, 320, hd)
+        values = rng.standard_normal(keys.shape, dtype=np.float32)
+        q_pre = rng.standard_normal((2, 8, 200, 64), dtype=np.float32)
+        q_dec = rng.standard_normal((4, 2, 8, 1, 64), dtype=np.float32)
+        return {"keys": keys, "values": values, "q_pre": q_pre, "q_dec": q_dec,
+                "steps": np.array([201, 255, 256, 257]), "thresholds": [0.05]}
     raise KeyError(name)
 
 
 CASES = ["mask_semantic", "mask_random", "mask_mixture_hd64", "v1_config1", "v2_f16",
          "v2_bf16_hd64", "v3_bf16", "v3_f32_g1", "paged_f32", "v2_fp8",
-         "norm_cache", "decode_gate"]
+         "norm_cache", "decode_gate", "hf_hook"]
 
 
 def fp8_quantize(keys_f32):

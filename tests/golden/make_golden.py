@@ -112,6 +112,20 @@ def main(ref_root: str, only=None) -> None:
                     m, qn = dg._pytorch_decode_gate(q, nrm, tau, 12, 4, 64, tight=tight)
                     out[f"evict_{i}_{int(tight)}"] = m.numpy()
                     out[f"qn_{i}_{int(tight)}"] = qn.numpy()
+        elif name == "hf_hook":
+            sys.path.insert(0, os.path.join(ref_root, "eval"))
+            import perplexity_eval as pev
+            from orthocache_gpu.norm_cache import SpectralNormCache
+            oca = pev.OrthoCache_GQA_Attention(tau=ths[0])
+            oca.norm_cache = SpectralNormCache(2, 8, torch.device("cpu"))
+            k, v = T(inp["keys"]), T(inp["values"])
+            out["prefill"] = oca.orthocache_attention(T(inp["q_pre"]), k[:, :, :200], v[:, :, :200], 4).numpy()
+            out["prefill_evicted"] = np.array(oca.stats["evicted_tiles"])
+            out["norms"] = oca.norm_cache.cache.numpy()
+            for i, n in enumerate(inp["steps"]):
+                before = oca.stats["decode_tiles_skipped"]
+                out[f"decode_{i}"] = oca.orthocache_attention(T(inp["q_dec"][i]), k[:, :, :n], v[:, :, :n], 4).numpy()
+                out[f"decode_skipped_{i}"] = np.array(oca.stats["decode_tiles_skipped"] - before)
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
         print("wrote", name)
 
