@@ -135,7 +135,9 @@ int oc_fused_attention_v3_gqa(const void* q, int q_dtype, int64_t q_seq_stride, 
  * reference's behaviour.  gate = OC_GATE_ZETA (threshold = zeta_max, the
  * reference's paged path) or OC_GATE_CAUCHY_SCHWARZ (threshold = tau).
  * block_size: power of two.  group = 1 with OC_GATE_ZETA is exactly the
- * reference's MHA paged kernel.  k_scale applies to float8 key caches only
+ * reference's MHA paged kernel.  num_splits is accepted for compatibility:
+ * the tiles of each (sequence, kv head) are processed in sequence order so
+ * that the block table is read in windows.  k_scale applies to float8 key caches only
  * (other dtypes: pass 1.0 and fold any scale into q): every key element is
  * de-quantised into q's dtype as round(float(k) * float(k_scale)) before the
  * gate and the logits, which is the reference's k_cache.to(q.dtype) * k_scale
@@ -230,6 +232,25 @@ int oc_fused_attention_cached(const void* q, int q_dtype, int64_t q_seq_stride, 
                               int64_t out_head_stride, float* m_out, float* l_out, float* acc_out,
                               uint8_t* evict_out, float* q_norms_out, uint32_t* retained, uint32_t* status,
                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Attention over explicit tile lists (no gate): each (sequence, kv head) g
+ * attends to the 64-token tiles tile_list[g * list_stride + k], k <
+ * list_count[g] (device int32 arrays; list_stride 0 shares one list).
+ * Entries must lie in [0, seq_len/64); an out-of-range entry reads a
+ * zero-filled tile (no access outside the tensor).  Shapes and the optional
+ * merged-state outputs as oc_fused_attention_cached.  Replaces the
+ * compacted-block attention of the reference's 'compact' pipeline mode
+ * (adaptive_attention.py:159-205, compaction.py:150-220), with 512-token
+ * blocks given as their 8 tiles. */
+int oc_fused_attention_tiles(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                             const void* keys, int k_dtype, int64_t k_seq_stride, int64_t k_head_stride,
+                             int64_t k_tok_stride, const void* values, int v_dtype, int64_t v_seq_stride,
+                             int64_t v_head_stride, int64_t v_tok_stride, int num_seqs, int num_kv_heads,
+                             int group, int64_t seq_len, int head_dim, const int32_t* tile_list,
+                             int64_t list_stride, const int32_t* list_count, int num_sms, void* out, int out_dtype,
+                             int64_t out_seq_stride, int64_t out_head_stride, float* m_out, float* l_out,
+                             float* acc_out, uint32_t* retained, uint32_t* status, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 /* Allocation-free variant of oc_fused_attention_v2 (no counterpart in the
  * reference).  For callers that cannot allocate device memory: code running

@@ -477,9 +477,13 @@ int oc_fused_attention_paged(const void* q, int q_dtype, int64_t q_seq_stride, i
   p.seq_lens = seq_lens;
   // the paged grid covers floor(max_blocks*block_size / 64) tiles per sequence
   const int64_t seq_len = tokens - tokens % 64;
+  // tiles of a unit are processed in sequence order (one split), so that each
+  // team's copies walk the block table forward and read it in windows;
+  // num_splits is accepted for compatibility and does not change the result
+  (void)num_splits;
   return v3_common(p, q, q_dtype, q_seq_stride, q_head_stride, k_cache, k_dtype, 0, k_head_stride, k_tok_stride,
                    v_cache, v_dtype, 0, v_head_stride, v_tok_stride, num_seqs, num_kv_heads, group, seq_len,
-                   head_dim, num_splits, num_sms, out, out_dtype, out_seq_stride, out_head_stride, mask_out,
+                   head_dim, 1, num_sms, out, out_dtype, out_seq_stride, out_head_stride, mask_out,
                    retained, status, workspace, workspace_bytes, stream);
 }
 
@@ -605,6 +609,37 @@ int oc_fused_attention_cached(const void* q, int q_dtype, int64_t q_seq_stride, 
                    k_tok_stride, values, v_dtype, v_seq_stride, v_head_stride, v_tok_stride, num_seqs,
                    num_kv_heads, group, seq_len, head_dim, 1, num_sms, out, out_dtype, out_seq_stride,
                    out_head_stride, nullptr, retained, status, workspace, base, stream);
+}
+
+int oc_fused_attention_tiles(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_head_stride,
+                             const void* keys, int k_dtype, int64_t k_seq_stride, int64_t k_head_stride,
+                             int64_t k_tok_stride, const void* values, int v_dtype, int64_t v_seq_stride,
+                             int64_t v_head_stride, int64_t v_tok_stride, int num_seqs, int num_kv_heads,
+                             int group, int64_t seq_len, int head_dim, const int32_t* tile_list,
+                             int64_t list_stride, const int32_t* list_count, int num_sms, void* out, int out_dtype,
+                             int64_t out_seq_stride, int64_t out_head_stride, float* m_out, float* l_out,
+                             float* acc_out, uint32_t* retained, uint32_t* status, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (!tile_list || !list_count || list_stride < 0) return OC_ERR_INVALID;
+  if ((acc_out != nullptr) != (m_out != nullptr) || (acc_out != nullptr) != (l_out != nullptr)) return OC_ERR_INVALID;
+  DecodeParams p = blank();
+  p.gate = oc::GATE_LIST;
+  p.tile_list = tile_list;
+  p.list_count = list_count;
+  p.list_stride = list_stride;
+  if (acc_out) {
+    p.sh_m = m_out;
+    p.sh_l = l_out;
+    p.sh_acc = acc_out;
+    return v3_common(p, q, q_dtype, q_seq_stride, q_head_stride, keys, k_dtype, k_seq_stride, k_head_stride,
+                     k_tok_stride, values, v_dtype, v_seq_stride, v_head_stride, v_tok_stride, num_seqs,
+                     num_kv_heads, group, seq_len, head_dim, 1, num_sms, nullptr, OC_F32, 0, head_dim, nullptr,
+                     retained, status, workspace, workspace_bytes, stream);
+  }
+  return v3_common(p, q, q_dtype, q_seq_stride, q_head_stride, keys, k_dtype, k_seq_stride, k_head_stride,
+                   k_tok_stride, values, v_dtype, v_seq_stride, v_head_stride, v_tok_stride, num_seqs,
+                   num_kv_heads, group, seq_len, head_dim, 1, num_sms, out, out_dtype, out_seq_stride,
+                   out_head_stride, nullptr, retained, status, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

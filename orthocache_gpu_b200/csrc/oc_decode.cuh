@@ -474,6 +474,15 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // completing on the slot's barrier.
   // The slot was only read (generic proxy) since its last copy, so the next
   // copy needs no proxy fence: __syncwarp orders the lanes' reads before it.
+  // Paged layout: block-table windows, one for the K copy cursor and one for
+  // the V copy cursor.  Lane i holds entry base + i of sequence wseq, loaded
+  // by one coalesced warp load; a tile's page ids are then read with a
+  // shuffle instead of a dependent global load per copy.  Tiles of a team are
+  // consecutive inside a unit (the paged path runs with one split), so a
+  // window of 32 pages serves 512 / 64 * page_size tokens.
+  int win_seq[2] = {-1, -1}, win_base[2] = {0, 0};
+  int win_val[2] = {0, 0};
+  const int max_pages = p.layout == LAYOUT_PAGED ? ((p.num_tiles * 64 + (1 << p.block_shift) - 1) >> p.block_shift) : 0;
   auto issue = [&](uint32_t s, int seq, int kvh, int tile, bool isv) {
     const uint32_t fbar = bar0 + 8u * s;
     const uint32_t dst = smem_u32(ring + s * SLOT);
@@ -496,6 +505,28 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     __syncwarp();
     const int RB = p.box_rows;
     const int nruns = 64 / RB;
+    if (nruns <= 32) {
+      const int w = isv ? 1 : 0;
+      const int first = (tile * 64) >> p.block_shift, last = (tile * 64 + 63) >> p.block_shift;
+      if (seq != win_seq[w] || first < win_base[w] || last >= win_base[w] + 32) {  // warp-uniform
+        win_seq[w] = seq;
+        win_base[w] = first;
+        const int e = first + lane;
+        win_val[w] = e < max_pages ? p.block_tables[(int64_t)seq * p.bt_seq_stride + e] : 0;
+      }
+      const int t = tile * 64 + (lane < nruns ? lane : 0) * RB;
+      int pb = __shfl_sync(0xffffffffu, win_val[w], (t >> p.block_shift) - win_base[w]);
+      if (lane < nruns) {
+        if (pb < 0 || pb >= p.num_blocks) {
+          atomicOr(p.status, ST_BAD_PAGE);
+          pb = 0;
+        }
+        const int tk = t & ((1 << p.block_shift) - 1);
+        tma_load_4d(dst + (uint32_t)(lane * RB * (row / P)), tm, panel * 64, crd(1, tk, kvh, pb),
+                    crd(2, tk, kvh, pb), crd(3, tk, kvh, pb), fbar, pol);
+      }
+      return;
+    }
     for (int run = lane; run < nruns; run += 32) {
       const int t = tile * 64 + run * RB;
       int pb = p.block_tables[(int64_t)seq * p.bt_seq_stride + (t >> p.block_shift)];

@@ -122,7 +122,7 @@ def fused_orthocache_attention_paged(
         "num_heads": num_heads,
         "num_seqs": num_seqs,
         "layout": "paged",
-        "tile_assignment": "interleaved",
+        "tile_assignment": "contiguous",
         "gate_type": "zeta" if tau is None else "cauchy_schwarz",
     }
     if return_mask:

@@ -11,8 +11,10 @@ decode modes on the hot path:
   (pipeline.py:438-439);
 * ``mode='dense'`` is the reference's dense einsum/softmax baseline
   (pipeline.py:558-568), in PyTorch;
-* ``mode='compact'`` (the 512-token block compaction path) is not part of
-  this library and raises ``NotImplementedError``.
+* ``mode='compact'`` is the 512-token block path: a two-gate block mask
+  (logit bound and ζ over 512-point Walsh bands) computed with PyTorch ops,
+  then one kernel launch attending only to the retained blocks
+  (``orthocache_gpu_b200.compact``).
 
 Like the reference, the fused mode decodes the first query token only and
 returns (1, num_heads, head_dim).  Its ``eviction_rate`` is the measured rate
@@ -82,8 +84,10 @@ class GPUProfile:
     compute_class: str = "datacenter"
 
 
+# crossover 512 as the reference's B200 entry (pipeline.py:192-196): below one
+# 512-token block the compact mode runs dense
 B200_PROFILE = GPUProfile(name="B200", sm_count=148, mem_bandwidth_gbps=6456.0, sram_per_sm_kb=228,
-                          crossover_seq_len=0, compute_class="hpc")
+                          crossover_seq_len=512, compute_class="hpc")
 
 
 def get_hardware_profile(device: torch.device | None = None) -> GPUProfile:
@@ -172,6 +176,28 @@ def orthocache_forward(
                 metadata["bypass_flags"] = int(flags)
         return output, metadata
 
-    raise NotImplementedError(
-        f"mode={mode!r}: orthocache_gpu_b200 implements the fused decode path ('triton_fused') and the "
-        "dense baseline ('dense'); the 512-token block compaction path ('compact') is not part of it")
+    hw = get_hardware_profile(q.device)
+    if seq_len_k < hw.crossover_seq_len:  # hardware-aware bypass (pipeline.py:397-421)
+        t0 = time.perf_counter()
+        output = _dense_attention(q, keys, values, head_dim)
+        if telemetry >= TelemetryLevel.FLAGS:
+            flags = BypassFlag.CROSSOVER_BYPASS
+            if hw.compute_class == "unknown":
+                flags |= BypassFlag.HW_AUTO_DETECTED
+            metadata["latency_ms"] = (time.perf_counter() - t0) * 1000
+            metadata["eviction_rate"] = 0.0
+            metadata["bypass_flags"] = int(flags)
+            metadata["crossover_threshold"] = hw.crossover_seq_len
+            metadata["gpu_profile"] = hw.name
+            if telemetry >= TelemetryLevel.VERBOSE:
+                metadata["crossover_reason"] = format_bypass_reason(flags, seq_len_k, hw.crossover_seq_len, hw)
+        return output, metadata
+
+    if mode == "compact":
+        from .compact import compact_forward
+        output, meta = compact_forward(q, keys, values, block_size, zeta_max, tau, {})
+        if telemetry != TelemetryLevel.SILENT:
+            metadata.update(meta)
+        return output, metadata
+
+    raise ValueError(f"Unknown mode: {mode!r}. Use 'dense', 'compact', or 'triton_fused'.")

@@ -138,12 +138,29 @@ def case_inputs(name: str) -> dict:
         q_dec = rng.standard_normal((4, 2, 8, 1, 64), dtype=np.float32)
         return {"keys": keys, "values": values, "q_pre": q_pre, "q_dec": q_dec,
                 "steps": np.array([201, 255, 256, 257]), "thresholds": [0.05]}
+    if name == "compact":
+        # orthocache_forward(mode='compact'): 8 blocks of 512 tokens, half of
+        # them low-sequency (the first 64 rows of the 512-point Walsh basis)
+        rng = np.random.default_rng(44)
+        w = walsh(512)[:, :64]
+        blocks = []
+        for b in range(8):
+            if b % 2 == 0:
+                coef = rng.standard_normal((64, 4 * 64), dtype=np.float32)
+                blk = w @ coef + np.float32(0.05) * rng.standard_normal((512, 4 * 64), dtype=np.float32)
+            else:
+                blk = rng.standard_normal((512, 4 * 64), dtype=np.float32)
+            blocks.append(blk.reshape(512, 4, 64))
+        keys = np.concatenate(blocks, 0).astype(np.float32)
+        values = rng.standard_normal(keys.shape, dtype=np.float32)
+        q = rng.standard_normal((4, 4, 64), dtype=np.float32)
+        return {"q": q, "keys": keys, "values": values, "thresholds": [1.0, 5.0, 50.0]}
     raise KeyError(name)
 
 
 CASES = ["mask_semantic", "mask_random", "mask_mixture_hd64", "v1_config1", "v2_f16",
          "v2_bf16_hd64", "v3_bf16", "v3_f32_g1", "paged_f32", "v2_fp8",
-         "norm_cache", "decode_gate", "hf_hook"]
+         "norm_cache", "decode_gate", "hf_hook", "compact"]
 
 
 def fp8_quantize(keys_f32):

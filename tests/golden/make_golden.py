@@ -126,6 +126,23 @@ def main(ref_root: str, only=None) -> None:
                 before = oca.stats["decode_tiles_skipped"]
                 out[f"decode_{i}"] = oca.orthocache_attention(T(inp["q_dec"][i]), k[:, :, :n], v[:, :, :n], 4).numpy()
                 out[f"decode_skipped_{i}"] = np.array(oca.stats["decode_tiles_skipped"] - before)
+        elif name == "compact":
+            # the reference's torch.compile wrappers need a host compiler: run them
+            # eagerly (TORCHDYNAMO_DISABLE=1 in the environment) -- same arithmetic
+            from orthocache_gpu import pipeline as ppl
+            from orthocache_gpu import spectral_energy as se
+            q, k, v = T(inp["q"]), T(inp["keys"]), T(inp["values"])
+            out["zeta"] = se.compute_spectral_decay_ratio(k).numpy()
+            out["bounds"] = se.compute_query_aware_bounds(q, k).numpy()
+            runs = [(1.0, None), (5.0, None), (50.0, 30.0), (50.0, 1e9)]
+            out["runs"] = np.array([[z, np.nan if t is None else t] for z, t in runs])
+            for i, (zm, tau) in enumerate(runs):
+                o, meta = ppl.orthocache_forward(q, k, v, mode="compact", zeta_max=zm, tau=tau)
+                out[f"out_{i}"] = o.float().numpy()
+                for key in ("tau", "zeta_mean", "zeta_std", "zeta_min", "zeta_max_observed", "blocks_retained",
+                            "perfect_eviction_blocks", "statistical_eviction_blocks", "perfect_eviction_rate",
+                            "eviction_rate"):
+                    out[f"{key}_{i}"] = np.array(meta[key])
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
         print("wrote", name)
 

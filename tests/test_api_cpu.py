@@ -111,9 +111,13 @@ def test_walsh_matrix_matches_oracle():
         np.testing.assert_array_equal(oc.generate_walsh_matrix(n).numpy(), orc.walsh_matrix(n))
 
 
-def test_pipeline_dense_mode_runs_on_cpu_and_compact_is_out_of_scope():
+def test_pipeline_dense_mode_and_compact_crossover_bypass_run_on_cpu():
     q, k, v = _t(1, 4, 64), _t(256, 4, 64), _t(256, 4, 64)
     out, meta = oc.orthocache_forward(q, k, v, mode="dense")
     assert out.shape == (1, 4, 64) and meta["actual_mode"] == "dense" and meta["eviction_rate"] == 0.0
-    with pytest.raises(NotImplementedError):
-        oc.orthocache_forward(q, k, v, mode="compact")
+    # shorter than the B200 crossover (512): compact mode attends densely and says so
+    out2, meta2 = oc.orthocache_forward(q, k, v, mode="compact", telemetry=oc.TelemetryLevel.VERBOSE)
+    assert torch.equal(out, out2) and meta2["bypass_flags"] & oc.BypassFlag.CROSSOVER_BYPASS
+    assert "crossover=512" in meta2["crossover_reason"]
+    with pytest.raises(ValueError, match="Unknown mode"):
+        oc.orthocache_forward(q, _t(1024, 4, 64), _t(1024, 4, 64), mode="bogus")

@@ -22,6 +22,16 @@ DEV = "cuda"
 QH_ATOL = 4e-3  # |q_high| of a query without high band: sqrt of float32 rounding noise
 
 
+def _mid_tau(q, norms, G, hd):
+    """A tau between two neighbouring per-tile bounds near their median (no tile near the threshold)."""
+    b = np.sort(np.concatenate([orc.decode_gate(qq, nn, 1.0, nn.shape[-1], G)[2].ravel()
+                                for qq, nn in zip(q.reshape(-1, *q.shape[-2:]), norms.reshape(-1, *norms.shape[-2:]))]))
+    i = len(b) // 2
+    while i + 1 < len(b) and b[i + 1] - b[i] < 1e-3 * b[i]:
+        i += 1
+    return float((b[i] + b[i + 1]) / 2) / (64 * hd)
+
+
 def T(a, dtype=torch.float32):
     return torch.from_numpy(np.ascontiguousarray(a)).to(dtype).to(DEV)
 
@@ -81,7 +91,7 @@ def test_cached_decode_against_oracle(q_stat, dt):
     x = gqa_inputs(2, 4, 2048, 128, seed=7, batch=3)
     q, k, v = (cast_np(a, dt) for a in (x.q, x.keys, x.values))
     norms = orc.tile_high_norms(k)                            # (3, 2, 32), band [48, 64)
-    tau = float(np.median(norms) * 6.0 / (64 * 128))          # evicts a good part of the tiles
+    tau = _mid_tau(q, norms, 4, 128)                          # about half the tiles evicted
     out, meta = oc.fused_orthocache_attention_cached(T(x.q, dt), T(x.keys, dt), T(x.values, dt), T(norms), tau, 4,
                                                      q_stat=q_stat, return_mask=True)
     kept = 0
@@ -104,7 +114,7 @@ def test_cached_decode_never_reads_evicted_tiles():
     dt = torch.bfloat16
     q, k, v = (cast_np(a, dt) for a in (x.q, x.keys, x.values))
     norms = orc.tile_high_norms(k)
-    tau = float(np.median(norms) * 6.0 / (64 * 128))
+    tau = _mid_tau(q, norms, 4, 128)
     ref, ev, bound = orc.cached_attention(q, k, v, norms, tau, 4)
     assert ev.any() and not ev.all() and not orc.near_threshold(bound, tau * 64 * 128).any()
     kd, vd = T(x.keys, dt), T(x.values, dt)
@@ -137,7 +147,7 @@ def test_cached_decode_with_a_norm_cache_object_and_longer_capacity():
     k = T(x.keys, dt)
     c = oc.SpectralNormCache(2, 64, DEV).populate_from_keys(k, oc.generate_walsh_matrix(64))
     nrm = as_np(c.cache)[:, :16]
-    tau = float(np.median(nrm) * 6.0 / (64 * 128))
+    tau = _mid_tau(cast_np(x.q, dt), nrm, 4, 128)
     out, meta = oc.fused_orthocache_attention_cached(T(x.q, dt), k, T(x.values, dt), c, tau, 4, return_mask=True)
     ref, ev, bound = orc.cached_attention(cast_np(x.q, dt), cast_np(x.keys, dt), cast_np(x.values, dt), nrm, tau, 4,
                                           forced=(orc.near_threshold(orc.decode_gate(cast_np(x.q, dt), nrm, tau, 16,
