@@ -70,6 +70,15 @@ const char* oc_status_string(int code);
 /* Library version, e.g. 100 for 0.1.0. */
 int oc_version(void);
 
+/* Diagnostics: a device buffer of unsigned 64-bit words that decode launches
+ * fill with per-team timelines (8 words a team: %globaltimer at entry, after
+ * the first copies were issued, at the first arrival and at exit; first and
+ * last flattened tile; K and V tiles processed) followed by 3 words per merge
+ * block (timer before and after its grid dependency wait).  Written only by
+ * a library built with OC_TRACE; NULL disables.  No counterpart in the
+ * reference. */
+void oc_debug_set_trace(void* buffer);
+
 /* Bytes of workspace for an attention call over `num_groups` (sequence,
  * kv-head) pairs with `group` query heads each, at most `num_tiles` 64-token
  * tiles per sequence, and `head_dim`.  The mask-only call needs none. */

@@ -40,18 +40,26 @@ def _deps():
         glob.glob(os.path.join(ROOT, "include", "*.h"))
 
 
-def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+def up_to_date(lib: str = LIB) -> bool:
+    if not os.path.exists(lib):
         return False
-    t = os.path.getmtime(LIB)
+    t = os.path.getmtime(lib)
     return all(os.path.getmtime(f) <= t for f in _deps())
 
 
-def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -> str:
-    """Compile (if needed) and return the path of the shared library."""
-    if not force and up_to_date():
-        return LIB
-    os.makedirs(OUT_DIR, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, jobs: int | None = None, out_dir: str | None = None,
+          defines: tuple = ()) -> str:
+    """Compile (if needed) and return the path of the shared library.
+
+    ``out_dir`` / ``defines`` build a variant elsewhere (e.g. with OC_TRACE,
+    the diagnostics timeline) without touching the in-tree library.
+    """
+    out = out_dir or OUT_DIR
+    lib_path = os.path.join(out, os.path.basename(LIB))
+    if not force and up_to_date(lib_path):
+        return lib_path
+    os.makedirs(out, exist_ok=True)
+    extra = [f"-D{d}" for d in defines]
     cc = nvcc()
     objs = []
 
@@ -59,10 +67,10 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     newest_header = max(os.path.getmtime(f) for f in headers)
 
     def compile_one(src):
-        obj = os.path.join(OUT_DIR, os.path.basename(src)[:-3] + ".o")
+        obj = os.path.join(out, os.path.basename(src)[:-3] + ".o")
         if not force and os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(src), newest_header):
             return obj
-        cmd = [cc, *ARCH, *FLAGS, "-c", src, "-o", obj]
+        cmd = [cc, *ARCH, *FLAGS, *extra, "-c", src, "-o", obj]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed on {src}:\n{r.stdout}\n{r.stderr}")
@@ -72,13 +80,13 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
 
     with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
         objs = list(ex.map(compile_one, _sources()))
-    tmp = LIB + ".tmp"
+    tmp = lib_path + ".tmp"
     cmd = [cc, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib_path)
+    return lib_path
 
 
 if __name__ == "__main__":

@@ -14,7 +14,8 @@ import threading
 import torch
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "_lib", "liborthocache_b200.so")
+# ORTHOCACHE_B200_LIB selects another build of the same C ABI (e.g. a diagnostics build)
+LIB_PATH = os.environ.get("ORTHOCACHE_B200_LIB") or os.path.join(_PKG, "_lib", "liborthocache_b200.so")
 
 OC_F32, OC_F16, OC_BF16, OC_F8E4M3 = 0, 1, 2, 3
 OC_GATE_ZETA, OC_GATE_CAUCHY_SCHWARZ = 0, 2
@@ -30,6 +31,7 @@ _vp, _i, _i64, _d, _sz = C.c_void_p, C.c_int, C.c_int64, C.c_double, C.c_size_t
 SIGNATURES = {
     "oc_status_string": (C.c_char_p, [_i]),
     "oc_version": (_i, []),
+    "oc_debug_set_trace": (None, [_vp]),
     "oc_workspace_bytes": (_sz, [_i64, _i, _i64, _i]),
     "oc_auto_num_splits": (_i, [_i64, _i]),
     "oc_fwht_eviction": (_i, [_vp, _i, _i64, _i, _i64, _d, _vp, _vp, _vp, _vp]),

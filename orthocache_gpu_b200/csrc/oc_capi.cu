@@ -126,15 +126,21 @@ bool make_map(CUtensorMap* m, const char* base, int dtype, int hd, bool tc, cons
   return r == CUDA_SUCCESS;
 }
 
+unsigned long long* g_trace = nullptr;  // diagnostics buffer (oc_debug_set_trace)
+
 int run(const DecodeParams& p0, int k_dtype, int v_dtype, int hd, bool attn, int sms, cudaStream_t st) {
   DecodeParams p = p0;
+  p.trace = g_trace;
   const int gc = gc_for_group(p.group);
   p.box_rows = p.layout == oc::LAYOUT_LINEAR ? 64 : ((1 << p.block_shift) < 64 ? (1 << p.block_shift) : 64);
   // tensor cores need 16-bit keys, values of the same type and, for attention,
   // queries of that type too (the logits are then exact products in fp32);
   // swizzled boxes start on 1024-byte boundaries, so at least 8 rows a box
+  // (queries are read as 32-bit pairs there: 4-byte aligned rows)
+  const bool q_pairs = (reinterpret_cast<uintptr_t>(p.q) & 3u) == 0 && (p.q_seq_stride & 1) == 0 &&
+                       (p.q_head_stride & 1) == 0;
   const bool tc = (k_dtype == OC_F16 || k_dtype == OC_BF16) && v_dtype == k_dtype && hd >= 64 &&
-                  (!attn || p.q_dtype == k_dtype) && p.box_rows >= 8;
+                  (!attn || (p.q_dtype == k_dtype && q_pairs)) && p.box_rows >= 8;
   // unswizzled boxes start on 128-byte boundaries
   if (!tc && ((p.box_rows * hd * elem_bytes(k_dtype)) % 128 || (attn && (p.box_rows * hd * elem_bytes(v_dtype)) % 128)))
     return OC_ERR_UNSUPPORTED;
@@ -241,6 +247,8 @@ const char* oc_status_string(int code) {
 }
 
 int oc_version(void) { return 100; }
+
+void oc_debug_set_trace(void* buffer) { g_trace = static_cast<unsigned long long*>(buffer); }
 
 size_t oc_workspace_bytes(int64_t num_groups, int group, int64_t num_tiles, int head_dim) {
   if (num_groups < 1 || group < 1 || num_tiles < 0 || head_dim < 1) return 0;

@@ -142,7 +142,16 @@ struct DecodeParams {
   const int* tile_list;
   const int* list_count;
   int64_t list_stride;
+  // diagnostics (written only in builds with OC_TRACE defined): per team 16
+  // timestamps / counters, then 3 per merge block; see oc_debug_set_trace
+  unsigned long long* trace;
 };
+
+__device__ __forceinline__ unsigned long long oc_clock() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 // ---------------------------------------------------------------- conversions
 // cvt2<N>(src, dst): N consecutive elements at src (shared memory) -> N/2
@@ -393,6 +402,11 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+#ifdef OC_TRACE
+  const unsigned long long tr_t0 = oc_clock();
+  unsigned long long tr_t1 = 0, tr_t2 = 0, tr_a = 0, tr_b = 0, tr_x[4] = {0, 0, 0, 0};
+  int tr_nk = 0, tr_nv = 0;
+#endif
   const int c = lane % C, rg = lane / C;
   static_assert(!TC || (CF::KB == 2 && CF::VB == 2 && HD >= 64 && GC <= 8), "tensor-core path");
   constexpr bool KBF16 = TC && (sizeof(KT) == 2) && !std::is_same<KT, __half>::value;
@@ -416,6 +430,10 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   float2* xch = reinterpret_cast<float2*>(smem + CF::OFF_XCH) + team * 2 * P;
   float* stg = reinterpret_cast<float*>(smem + CF::OFF_STG) + warp * 64;  // finalize staging
   const uint32_t bar0 = smem_u32(smem + CF::OFF_BAR) + 8u * warp * NSLOT;  // this warp's slot barriers
+  if (tid == 0) {  // fetch the copy descriptors while the prologue runs
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmK) : "memory");
+    if (ATTN) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmV) : "memory");
+  }
   if (lane < NSLOT) mbar_init(bar0 + 8u * lane, 1);
   mbar_init_fence();
   __syncwarp();
@@ -435,8 +453,37 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     }
     tp[u + 1] = T;
   }
-  block_scan(tp, U, scan_tmp);
+#ifdef OC_TRACE
+  __syncwarp();
+  tr_a = oc_clock();
+#endif
+  if (U <= 32 * 32) {  // one warp scans (up to 32 values a lane)
+    __syncthreads();
+    if (warp == 0) {
+      const int per = (U + 31) / 32, lo = 1 + lane * per, hi = min(U + 1, lo + per);
+      int run = 0;
+      for (int i = lo; i < hi; ++i) run += tp[i];
+      int inc = run;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      int base = inc - run;
+      for (int i = lo; i < hi; ++i) {
+        base += tp[i];
+        tp[i] = base;
+      }
+      if (lane == 0) tp[0] = 0;
+    }
+    __syncthreads();
+  } else {
+    block_scan(tp, U, scan_tmp);
+  }
   const int64_t N = tp[U];
+#ifdef OC_TRACE
+  tr_x[0] = oc_clock();
+#endif
   if (ATTN && blockIdx.x == 0)
     for (int u = tid; u <= U; u += blockDim.x) p.tile_prefix[u] = tp[u];
 
@@ -628,6 +675,9 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // tiles in the range are gated and no V copy of it is pending: directly when
   // the range holds the whole unit, else as a partial state for merge_kernel.
   const int64_t WE = (N < W) ? (N > 0 ? N : 1) : W;  // warps with a tile range
+#ifdef OC_TRACE
+  tr_x[1] = oc_clock();
+#endif
   const bool active = wg < WE;
   const int64_t fa = active ? range_lo(wg, N, WE) : 0, fb = active ? range_lo(wg + 1, N, WE) : 0;
   int kept_stat = 0;
@@ -642,6 +692,9 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
             emit(p, seq, kvh * p.group + chunk * GC + g, d, -1e9f, 0.f, 0.f);
       }
   }
+#ifdef OC_TRACE
+    tr_x[2] = oc_clock();
+#endif
     float m_run[GC], l_part[GC];
     float2 acc[TC ? 1 : GC][D2];
     // tensor-core path: this lane's query g8 (m, partial l) and O^T fragments
@@ -766,17 +819,30 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   uint32_t qf_pf[TC ? HDL / 16 : 1][2];  // prefetched fragments of unit pf_unit
   int pf_unit = -1;
   // q rows of a unit's query chunk (this warp's panel) as raw 16-bit mma B fragments
-  auto load_qf = [&](int seq, int kvh, int chunk, uint32_t (&dst)[TC ? HDL / 16 : 1][2]) {
+  // The loads are issued unconditionally (lanes without a query read the
+  // chunk's first head) and nothing consumes them here, so the warp does not
+  // wait for them: qf_apply masks the lanes without a query when the
+  // fragments are first used.  q rows are 4-byte aligned (checked on the host).
+  auto load_qf = [&](int seq, int kvh, int chunk, uint32_t (&dst)[TC ? HDL / 16 : 1][2], bool& ok) {
     if constexpr (TC) {
       const int hq = chunk * GC + g8;
-      const bool ok = g8 < GC && hq < p.group;
-      const uint16_t* qrow = static_cast<const uint16_t*>(p.q) + (int64_t)seq * p.q_seq_stride +
-                             (int64_t)(kvh * p.group + hq) * p.q_head_stride + panel * HDL;
+      ok = g8 < GC && hq < p.group;
+      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+          static_cast<const uint16_t*>(p.q) + (int64_t)seq * p.q_seq_stride +
+          (int64_t)(kvh * p.group + (ok ? hq : chunk * GC)) * p.q_head_stride + panel * HDL);
 #pragma unroll
       for (int ks = 0; ks < HDL / 16; ++ks) {
-        dst[ks][0] = ok ? (uint32_t)qrow[16 * ks + 2 * t4] | ((uint32_t)qrow[16 * ks + 2 * t4 + 1] << 16) : 0u;
-        dst[ks][1] = ok ? (uint32_t)qrow[16 * ks + 2 * t4 + 8] | ((uint32_t)qrow[16 * ks + 2 * t4 + 9] << 16) : 0u;
+        dst[ks][0] = qrow[8 * ks + t4];
+        dst[ks][1] = qrow[8 * ks + t4 + 4];
       }
+    }
+  };
+  bool qok_pf = false;
+  auto qf_apply = [&](const uint32_t (&src)[TC ? HDL / 16 : 1][2], bool ok) {
+#pragma unroll
+    for (int ks = 0; ks < (TC ? HDL / 16 : 1); ++ks) {
+      qf[ks][0] = ok ? src[ks][0] : 0u;
+      qf[ks][1] = ok ? src[ks][1] : 0u;
     }
   };
 
@@ -784,6 +850,9 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // V copy flag, unit and tile index
   //   dsc_a = 2 * (f - fa) + (V copy), or -1 for an empty slot; dsc_b = (unit << 20) | tile
   int dsc_a = -1, dsc_b = 0;
+#ifdef OC_TRACE
+  tr_x[3] = oc_clock();
+#endif
   const int u_first = (fb > fa) ? upper_index(tp, U, fa) : 0;
   int u_iss = u_first, seq_iss = 0, kvh_iss = 0;
   int64_t u_end_iss = 0;  // first flattened tile after unit u_iss
@@ -800,12 +869,15 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     seq_iss = unit_seq(u);
     kvh_iss = unit_kvh(u);
     if constexpr (ATTN && TC) {
-      load_qf(seq_iss, kvh_iss, unit_chunk(u), qf_pf);
+      load_qf(seq_iss, kvh_iss, unit_chunk(u), qf_pf, qok_pf);
       pf_unit = u;
     }
     it_iss.init((int)(f - tp[u]), tp[u + 1] - tp[u], S);
     if (p.tile_list != nullptr) list_pf = list_load(u, f);
   };
+#ifdef OC_TRACE
+  tr_b = oc_clock();
+#endif
   if (fb > fa) enter_unit(u_first, fa);
   auto issue_next = [&](uint32_t s) {
     if (f_iss < fb) {
@@ -828,6 +900,9 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     }
   };
   for (uint32_t s = 0; s < NSLOT; ++s) issue_next(s);
+#ifdef OC_TRACE
+  tr_t1 = oc_clock();
+#endif
 
   int u_k = -1, kept_k = 0;  // unit of the last gated K tile and its retained tiles in the range
   int seq_k = 0, kvh_k = 0, chunk_k = 0;
@@ -848,6 +923,10 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       continue;
     }
     unsigned char* ts = wait_slot(s);
+#ifdef OC_TRACE
+    if (tr_t2 == 0) tr_t2 = oc_clock();
+    if (isv) ++tr_nv; else ++tr_nk;
+#endif
     float* lgs = lgs_base + s * (CF::LGB / 4);
     if (!isv) {
       // ================================================ K tile: gate (+ logits)
@@ -866,13 +945,12 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
           const int64_t qb = (int64_t)seq * p.q_seq_stride;
           if constexpr (TC) {
             if (u == pf_unit) {  // fragments prefetched when the copy cursor entered the unit
-#pragma unroll
-              for (int ks = 0; ks < HDL / 16; ++ks) {
-                qf[ks][0] = qf_pf[ks][0];
-                qf[ks][1] = qf_pf[ks][1];
-              }
+              qf_apply(qf_pf, qok_pf);
             } else {
-              load_qf(seq, kvh, chunk, qf);
+              bool ok;
+              uint32_t tmp[TC ? HDL / 16 : 1][2];
+              load_qf(seq, kvh, chunk, tmp, ok);
+              qf_apply(tmp, ok);
             }
           } else {
 #pragma unroll
@@ -1255,6 +1333,14 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   }
   // this CTA's decode work is issued: the merge grid may be scheduled (its
   // griddepcontrol.wait still waits for the whole grid to complete)
+#ifdef OC_TRACE
+  if (p.trace != nullptr && panel == 0 && lane == 0) {
+    unsigned long long* r = p.trace + 16 * wg;
+    r[0] = tr_t0; r[1] = tr_t1; r[2] = tr_t2; r[3] = oc_clock();
+    r[4] = tr_a; r[5] = tr_b; r[6] = tr_nk; r[7] = tr_nv;
+    for (int i = 0; i < 4; ++i) r[8 + i] = tr_x[i];
+  }
+#endif
   if constexpr (ATTN) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
@@ -1267,7 +1353,16 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 template <int HD, int GC, int P>
 __global__ void __launch_bounds__(128) merge_kernel(const DecodeParams p, int64_t W) {
   constexpr int HDL = HD / P, PST = HDL + 4;
+#ifdef OC_TRACE
+  const unsigned long long tr_m0 = oc_clock();
+#endif
   asm volatile("griddepcontrol.wait;" ::: "memory");
+#ifdef OC_TRACE
+  if (p.trace != nullptr && threadIdx.x == 0) {
+    p.trace[16 * W + 3 * blockIdx.x] = tr_m0;
+    p.trace[16 * W + 3 * blockIdx.x + 1] = oc_clock();
+  }
+#endif
   const int lane = threadIdx.x & 31;
   const int64_t item = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int nchunks = (p.group + GC - 1) / GC;
