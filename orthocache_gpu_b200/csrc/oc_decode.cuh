@@ -406,6 +406,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   const unsigned long long tr_t0 = oc_clock();
   unsigned long long tr_t1 = 0, tr_t2 = 0, tr_a = 0, tr_b = 0, tr_x[4] = {0, 0, 0, 0};
   int tr_nk = 0, tr_nv = 0;
+  unsigned long long tr_wait = 0, tr_sync = 0;
 #endif
   const int c = lane % C, rg = lane / C;
   static_assert(!TC || (CF::KB == 2 && CF::VB == 2 && HD >= 64 && GC <= 8), "tensor-core path");
@@ -416,7 +417,13 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   const int64_t W = (int64_t)gridDim.x * (NW / P);        // teams in the grid
   const int64_t wg = (int64_t)blockIdx.x * (NW / P) + team;  // this warp's team
   auto team_sync = [&]() {
+#ifdef OC_TRACE
+    const unsigned long long c0 = oc_clock();
+#endif
     if constexpr (P > 1) asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "r"(32 * P) : "memory");
+#ifdef OC_TRACE
+    tr_sync += oc_clock() - c0;
+#endif
   };
   const int nchunks = (p.group + GC - 1) / GC;
   const int U = p.num_seqs * p.num_kv_heads * nchunks;
@@ -590,8 +597,14 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // Wait for the copy in slot s (bounded; a timeout sets the status bit).
   uint32_t phases = 0;  // bit s: parity of slot s's next completion
   auto wait_slot = [&](uint32_t s) {
+#ifdef OC_TRACE
+    const unsigned long long c0 = oc_clock();
+#endif
     if (!mbar_wait_bounded(bar0 + 8u * s, (phases >> s) & 1u, kWaitLimit) && lane == 0)
       atomicOr(p.status, ST_TIMEOUT);
+#ifdef OC_TRACE
+    tr_wait += oc_clock() - c0;
+#endif
     phases ^= 1u << s;
     __syncwarp();
     return ring + s * SLOT;
@@ -679,7 +692,8 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   tr_x[1] = oc_clock();
 #endif
   const bool active = wg < WE;
-  const int64_t fa = active ? range_lo(wg, N, WE) : 0, fb = active ? range_lo(wg + 1, N, WE) : 0;
+  // flattened tile indices fit in 32 bits (at most 2048 units of 2^20 tiles): the loop uses int
+  const int fa = active ? (int)range_lo(wg, N, WE) : 0, fb = active ? (int)range_lo(wg + 1, N, WE) : 0;
   int kept_stat = 0;
   if constexpr (ATTN) {
     // units without a tile: zero output (or an empty partial state)
@@ -855,15 +869,15 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 #endif
   const int u_first = (fb > fa) ? upper_index(tp, U, fa) : 0;
   int u_iss = u_first, seq_iss = 0, kvh_iss = 0;
-  int64_t u_end_iss = 0;  // first flattened tile after unit u_iss
-  int64_t f_iss = fa;
+  int u_end_iss = 0;  // first flattened tile after unit u_iss
+  int f_iss = fa;
   SplitIter it_iss;
   // GATE_LIST: list entry of the next tile to issue, loaded one issue ahead
   int list_pf = 0;
-  auto list_load = [&](int u, int64_t f) {
+  auto list_load = [&](int u, int f) {
     return p.tile_list[(int64_t)(u / nchunks) * p.list_stride + (f - tp[u])];
   };
-  auto enter_unit = [&](int u, int64_t f) {  // issue cursor enters unit u at flattened tile f
+  auto enter_unit = [&](int u, int f) {  // issue cursor enters unit u at flattened tile f
     u_iss = u;
     u_end_iss = tp[u + 1];
     seq_iss = unit_seq(u);
@@ -906,16 +920,16 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 
   int u_k = -1, kept_k = 0;  // unit of the last gated K tile and its retained tiles in the range
   int seq_k = 0, kvh_k = 0, chunk_k = 0;
-  int64_t f_gated = fa;              // K tiles [fa, f_gated) are gated
+  int f_gated = fa;                  // K tiles [fa, f_gated) are gated
   int acc_unit = -1;                 // unit held by the accumulator
-  int64_t uend_k = 0, ua_acc = 0, uend_acc = 0;  // range of the K unit / accumulator unit in [fa, fb)
+  int uend_k = 0, ua_acc = 0, uend_acc = 0;  // range of the K unit / accumulator unit in [fa, fb)
 
   for (uint32_t j = 0;; ++j) {
     const uint32_t s = j % NSLOT;
     if (!__any_sync(0xffffffffu, lane < NSLOT && dsc_a >= 0)) break;
     const int da = __shfl_sync(0xffffffffu, dsc_a, s);
     const int db = __shfl_sync(0xffffffffu, dsc_b, s);
-    const int64_t f = da < 0 ? -1 : fa + (da >> 1);
+    const int f = da < 0 ? -1 : fa + (da >> 1);
     const int isv = da & 1;
     const int u = db >> 20, tile = db & ((1 << 20) - 1);
     if (f < 0) {
@@ -1174,7 +1188,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         issue_next(s);
       }
       if constexpr (ATTN) {
-        const int64_t uend = uend_k;
+        const int uend = uend_k;
         if (f + 1 == uend && kept_k == 0) finalize(u, true);
       }
     } else {
@@ -1314,7 +1328,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     }
     if constexpr (ATTN) {
       if (acc_unit >= 0) {
-        const int64_t ua = ua_acc, uend = uend_acc;
+        const int ua = ua_acc, uend = uend_acc;
         if (f_gated >= uend &&
             !__any_sync(0xffffffffu, lane < NSLOT && dsc_a >= 0 && (dsc_a & 1) && fa + (dsc_a >> 1) >= ua &&
                                          fa + (dsc_a >> 1) < uend)) {
@@ -1339,6 +1353,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     r[0] = tr_t0; r[1] = tr_t1; r[2] = tr_t2; r[3] = oc_clock();
     r[4] = tr_a; r[5] = tr_b; r[6] = tr_nk; r[7] = tr_nv;
     for (int i = 0; i < 4; ++i) r[8 + i] = tr_x[i];
+    r[12] = tr_wait; r[13] = tr_sync;
   }
 #endif
   if constexpr (ATTN) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
