@@ -176,14 +176,19 @@ int oc_lse_merge(const float* m, const float* l, const float* acc, int64_t num_u
  * instead of the final output it writes this shard's merged partial state
  * m_out (units), l_out (units), acc_out (units, head_dim), units =
  * num_kv_heads*group, for oc_lse_merge across shards.  The tau gate and the
- * tile grid are those of the full sequence restricted to this shard. */
+ * tile grid are those of the full sequence restricted to this shard.
+ * seq_len_dev (nullable, one device int32, a multiple of 64 <= seq_len):
+ * the number of tokens to decode, read by the kernel, so that a launch
+ * captured in a CUDA graph can follow a growing cache (seq_len is then the
+ * capacity). */
 int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_stride, const void* keys,
                                 int k_dtype, int64_t k_head_stride, int64_t k_tok_stride,
                                 const void* values, int v_dtype, int64_t v_head_stride,
                                 int64_t v_tok_stride, int num_kv_heads, int group, int64_t seq_len,
                                 int head_dim, double tau, int num_splits, int num_sms, float* m_out,
-                                float* l_out, float* acc_out, uint8_t* mask_out, uint32_t* retained,
-                                uint32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+                                float* l_out, float* acc_out, uint8_t* mask_out, const int32_t* seq_len_dev,
+                                uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
+                                void* stream);
 
 /* ---- spectral norm cache and the O(1) decode gate ----------------------
  * Reference: src/orthocache_gpu/norm_cache.py:21-146 (SpectralNormCache),

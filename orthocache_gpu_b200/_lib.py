@@ -58,7 +58,7 @@ SIGNATURES = {
                                       _vp, _vp, _vp, _sz, _vp]),
     "oc_lse_merge": (_i, [_vp, _vp, _vp, _i64, _i, _i, _vp, _i, _vp]),
     "oc_fused_attention_v3_shard": (_i, [_vp, _i, _i64, _vp, _i, _i64, _i64, _vp, _i, _i64, _i64, _i, _i, _i64,
-                                         _i, _d, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+                                         _i, _d, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
 }
 
 _lib = None

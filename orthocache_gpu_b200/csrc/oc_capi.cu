@@ -427,10 +427,11 @@ int oc_fused_attention_v3_shard(const void* q, int q_dtype, int64_t q_head_strid
                                 int64_t v_head_stride, int64_t v_tok_stride, int num_kv_heads, int group,
                                 int64_t seq_len, int head_dim, double tau, int num_splits, int num_sms,
                                 float* m_out, float* l_out, float* acc_out, uint8_t* mask_out,
-                                uint32_t* retained, uint32_t* status, void* workspace, size_t workspace_bytes,
-                                void* stream) {
+                                const int32_t* seq_len_dev, uint32_t* retained, uint32_t* status,
+                                void* workspace, size_t workspace_bytes, void* stream) {
   if (!m_out || !l_out || !acc_out) return OC_ERR_INVALID;
   DecodeParams p = blank();
+  p.seq_lens = seq_len_dev;  // nullable: tokens actually decoded, read on the device
   p.gate = oc::GATE_CS;
   p.thr = round_down_f32(tau);
   p.sh_m = m_out;

@@ -42,12 +42,15 @@ def shard_range(seq_len: int, world_size: int, rank: int, tile_size: int = TILE_
 
 def shard_partials(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, tau: float,
                    num_query_groups: int, num_splits: Optional[int] = None,
-                   k_scale: float = 1.0, stats: bool = True) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, int]:
+                   k_scale: float = 1.0, stats: bool = True,
+                   seq_len_dev: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, int]:
     """This rank's merged state over its K / V shard.
 
     q (Hq, hd); keys / values (KVH, S_shard, hd).  Returns float32 tensors
     m (Hq,), l (Hq,), acc (Hq, hd) and the number of retained tiles (-1 with
-    ``stats=False``, which skips that host synchronisation).
+    ``stats=False``, which skips that host synchronisation).  ``seq_len_dev``
+    (one int32 on the device, a multiple of 64): decode only that many leading
+    tokens of keys / values, read by the kernel (CUDA-graph friendly).
     """
     num_kv_heads, seq_len, head_dim = keys.shape
     G = num_query_groups
@@ -77,7 +80,8 @@ def shard_partials(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, ta
         keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1),
         values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1),
         num_kv_heads, G, seq_len, head_dim, float(tau), num_splits, _lib.num_sms(dev),
-        m.data_ptr(), l.data_ptr(), acc.data_ptr(), 0, ws.retained_ptr if stats else 0, ws.status_ptr,
+        m.data_ptr(), l.data_ptr(), acc.data_ptr(), 0, _lib.ptr(seq_len_dev), ws.retained_ptr if stats else 0,
+        ws.status_ptr,
         wptr, wbytes, stream), "oc_fused_attention_v3_shard")
     return m, l, acc, (_lib.read_stats(ws) if stats else -1)
 

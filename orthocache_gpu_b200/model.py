@@ -84,7 +84,9 @@ class GatedLlama:
                        for _ in range(s.layers)]
         self.norm = ones(s.hidden)
         self.lm_head = w(s.hidden, s.vocab)
-        self.k_cache = [torch.zeros(s.kv_heads, max_len, s.head_dim, device=self.dev, dtype=dtype)
+        # token-major caches (max_len, kv_heads, head_dim): a prefix [:n] is contiguous (what dense
+        # flash-decoding wants); the fused kernel reads the (kv_heads, n, head_dim) view through its strides
+        self.k_cache = [torch.zeros(max_len, s.kv_heads, s.head_dim, device=self.dev, dtype=dtype)
                         for _ in range(s.layers)]
         self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
         self.length = 0
@@ -119,8 +121,8 @@ class GatedLlama:
         x = self.embed[tokens]
         for i, L in enumerate(self.layers):
             q, k, v = self._qkv(L, _rms(x, L["ln1"], s.eps), pos)
-            self.k_cache[i][:, :T] = k
-            self.v_cache[i][:, :T] = v
+            self.k_cache[i][:T] = k.transpose(0, 1)
+            self.v_cache[i][:T] = v.transpose(0, 1)
             a = F.scaled_dot_product_attention(q[None], k[None], v[None], is_causal=True, enable_gqa=True)[0]
             x = x + a.transpose(0, 1).reshape(T, -1) @ L["wo"]
             x = self._mlp(L, x)
@@ -143,11 +145,11 @@ class GatedLlama:
         G = s.heads // s.kv_heads
         n = self.length
         full = n - n % 64
-        kc, vc = self.k_cache[i], self.v_cache[i]
+        kc, vc = self.k_cache[i].transpose(0, 1), self.v_cache[i].transpose(0, 1)  # (kv_heads, max_len, hd) views
         scale = LOG2E / math.sqrt(s.head_dim)
         if tau_mode == "flash":  # dense flash-decoding of every cached token (the fair dense arm)
             import flashinfer
-            return flashinfer.single_decode_with_kv_cache(q, kc[:, :n], vc[:, :n], kv_layout="HND")
+            return flashinfer.single_decode_with_kv_cache(q, self.k_cache[i][:n], self.v_cache[i][:n], kv_layout="NHD")
         if tau_mode is None or full == 0:  # dense (reference point, or no whole tile yet)
             a = F.scaled_dot_product_attention(q[None, :, None], kc[None, :, :n], vc[None, :, :n], enable_gqa=True)
             return a[0, :, 0]
@@ -175,8 +177,8 @@ class GatedLlama:
         x = self.embed[token]
         for i, L in enumerate(self.layers):
             q, k, v = self._qkv(L, _rms(x, L["ln1"], s.eps), pos)
-            self.k_cache[i][:, self.length] = k[:, 0]
-            self.v_cache[i][:, self.length] = v[:, 0]
+            self.k_cache[i][self.length] = k[:, 0]
+            self.v_cache[i][self.length] = v[:, 0]
             self.length += 1
             a = self._attend(i, q[:, 0].contiguous(), tau_mode)
             self.length -= 1
@@ -184,6 +186,93 @@ class GatedLlama:
             x = self._mlp(L, x)
         self.length += 1
         return _rms(x, self.norm, s.eps) @ self.lm_head
+
+    # ---------------------------------------------------------------- CUDA-graph decode
+    def _attend_dev(self, i, q, npos, full_dev):
+        """Decode attention with device-side lengths: npos (1,) int64 tokens in the cache,
+        full_dev (1,) int32 = npos rounded down to whole tiles.  Every shape is fixed,
+        so a step built from it can be captured once and replayed."""
+        s = self.s
+        G = s.heads // s.kv_heads
+        kc, vc = self.k_cache[i].transpose(0, 1), self.v_cache[i].transpose(0, 1)
+        cap = self.max_len - self.max_len % 64
+        m, l, acc, _ = shard_partials(q, kc[:, :cap], vc[:, :cap], self.tau[i], G, stats=False,
+                                      seq_len_dev=full_dev)
+        # the ragged tail: the 64 slots after the whole tiles, those at or beyond npos masked
+        idx = full_dev.long() + torch.arange(64, device=self.dev)
+        valid = idx < npos
+        idx = idx.clamp(max=self.max_len - 1)
+        kt = kc.index_select(1, idx).repeat_interleave(G, 0).float()      # (Hq, 64, hd)
+        vt = vc.index_select(1, idx).repeat_interleave(G, 0).float()
+        sc = (kt @ q.float()[:, :, None])[..., 0] * (LOG2E / math.sqrt(s.head_dim))
+        sc = sc.masked_fill(~valid[None], float("-inf"))
+        mt = sc.amax(-1).clamp(min=-1e9)                                 # an empty tail weighs 0
+        pt = torch.exp2(sc - mt[:, None])
+        return merge_states(torch.stack([m, mt], 1).contiguous(), torch.stack([l, pt.sum(-1)], 1).contiguous(),
+                            torch.stack([acc, (pt[:, None, :] @ vt)[:, 0]], 1).contiguous(), self.dtype)
+
+    @torch.no_grad()
+    def _step_dev(self, tok, npos):
+        """One decode step from device state: tok (1,) next token, npos (1,) cache length;
+        both are updated in place (argmax token, length + 1)."""
+        s = self.s
+        x = self.embed[tok]
+        n1 = npos + 1
+        full_dev = (torch.div(n1, 64, rounding_mode="floor") * 64).to(torch.int32)
+        for i, L in enumerate(self.layers):
+            q, k, v = self._qkv(L, _rms(x, L["ln1"], s.eps), npos)
+            self.k_cache[i].index_copy_(0, npos, k.transpose(0, 1))
+            self.v_cache[i].index_copy_(0, npos, v.transpose(0, 1))
+            a = self._attend_dev(i, q[:, 0].contiguous(), n1, full_dev)
+            x = x + a.reshape(1, -1) @ L["wo"]
+            x = self._mlp(L, x)
+        logits = _rms(x, self.norm, s.eps) @ self.lm_head
+        tok.copy_(logits.argmax(-1))
+        npos.add_(1)
+        return logits
+
+    @torch.no_grad()
+    def generate_graph(self, prompt: torch.Tensor, steps: int, tau_mode="median") -> Dict:
+        """Greedy decoding with each decode step replayed from one captured CUDA graph.
+
+        Prefill and the first step run eagerly (the first step calibrates each
+        layer's tau); the step is then captured once and replayed ``steps - 1``
+        times, with lengths and tokens kept on the device (no host sync per token).
+        Returns the per-step device time (CUDA events around the replays).
+        """
+        self.length = 0
+        self.tau = [None] * self.s.layers
+        logits = self.prefill(prompt)
+        tok = logits.argmax(-1)
+        first = self.step(tok, tau_mode)            # eager: sets self.tau
+        tok_d = first.argmax(-1).reshape(1).clone()
+        npos = torch.full((1,), self.length, dtype=torch.long, device=self.dev)
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st):
+            # a warm-up step outside the capture (workspaces, tensor maps), undone afterwards
+            t0, n0 = tok_d.clone(), npos.clone()
+            self._step_dev(tok_d, npos)
+            tok_d.copy_(t0)
+            npos.copy_(n0)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=st):
+                self._step_dev(tok_d, npos)
+        torch.cuda.current_stream().wait_stream(st)
+        toks = [int(tok), int(tok_d)]
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        hist = []
+        for _ in range(steps - 1):
+            g.replay()
+            hist.append(tok_d.clone())
+        b.record()
+        torch.cuda.synchronize()
+        toks += [int(t) for t in hist]
+        self.length = int(npos)
+        ms = a.elapsed_time(b) / max(1, steps - 1)
+        return {"tokens": toks, "ms_per_token": ms, "tau": self.tau, "final_length": self.length}
 
     @torch.no_grad()
     def generate(self, prompt: torch.Tensor, steps: int, tau_mode="median") -> Dict:

@@ -15,7 +15,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def declared_symbols():
     src = open(os.path.join(ROOT, "include", "orthocache_b200.h")).read()
-    return sorted(set(re.findall(r"^\s*(?:const char\*|int|size_t)\s+(oc_\w+)\(", src, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:const char\*|int|size_t|void)\s+(oc_\w+)\(", src, re.M)))
 
 
 def test_header_declares_the_reference_entry_points():

@@ -49,3 +49,42 @@ def test_median_tau_generates():
     assert len(res["tokens"]) == 9 and res["final_length"] == 648
     assert all(t is not None and t > 0 for t in res["tau"])
     assert res["ms_per_token"] > 0
+
+
+def test_device_length_step_matches_eager_step_and_graph_generation_runs():
+    m = _model(1024)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2)
+    prompt = torch.randint(0, SHAPE["vocab"], (700,), generator=g, device="cuda")
+    m.length = 0
+    m.tau = [None] * SHAPE["layers"]
+    tok = m.prefill(prompt).argmax(-1)
+    m.step(tok, "median")                        # calibrates tau, length 701
+    kc = [k.clone() for k in m.k_cache]
+    vc = [v.clone() for v in m.v_cache]
+    n0 = m.length
+    ref = m.step(tok, "median").float()           # eager step at length 701 -> 702
+    for i in range(SHAPE["layers"]):
+        m.k_cache[i].copy_(kc[i])
+        m.v_cache[i].copy_(vc[i])
+    npos = torch.full((1,), n0, dtype=torch.long, device="cuda")
+    t = tok.reshape(1).clone()
+    got = m._step_dev(t, npos).float()
+    assert int(npos) == n0 + 1
+    err = (got - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item() + 1e-3, err
+    res = m.generate_graph(prompt, 20, tau_mode="median")
+    assert len(res["tokens"]) == 21 and res["final_length"] == 700 + 20 and res["ms_per_token"] > 0
+
+
+def test_flash_dense_arm_matches_sdpa_dense():
+    m = _model(512)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    prompt = torch.randint(0, SHAPE["vocab"], (200,), generator=g, device="cuda")
+    outs = {}
+    for mode in (None, "flash"):
+        m.length = 0
+        tok = m.prefill(prompt).argmax(-1)
+        outs[mode] = m.step(tok, mode).float()
+    assert (outs[None] - outs["flash"]).abs().max().item() <= 2e-2 * outs[None].abs().max().item() + 1e-3
