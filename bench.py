@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only: no sweep, e2e or CPU baseline (profiling target)")
+    ap.add_argument("--workload", default="v2", choices=["v2", "v3", "paged", "cached"],
+                    help="with --quick: the configuration to time (profiling targets of the other kernels)")
+    ap.add_argument("--num-seqs", type=int, default=16, help="with --quick: sequences of the v3/paged/cached case")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-sample-heads", type=int, default=0, help="0 = auto (about 10-30 s of CPU work)")
     return ap.parse_args()
@@ -246,6 +249,69 @@ def _line(name, us, nbytes, evict, peak, extra=None):
          "evict": round(evict, 3), "algorithmic_bytes": int(nbytes)}
     d.update(extra or {})
     return d
+
+
+def quick_workload(a, dev):
+    """One configuration timed alone (graph-replayed), for profiling its kernel.
+
+    v3 / cached: a.num_seqs sequences of the V3 configuration (8 kv heads,
+    G 4, 32K, bf16, tau 150; cached: the norm-cache gate at the median
+    bound); paged: the first a.num_seqs sequences of the paged configuration
+    (16-token pages, tau 150).  Prints one JSON line.
+    """
+    import orthocache_gpu_b200 as oc
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    KVH, G, HD, TAU = 8, 4, 128, 150.0
+    if a.workload in ("v3", "cached"):
+        B, S = a.num_seqs, 32768
+        k = _mixture_device((B, KVH), S, HD, g, dev).to(torch.bfloat16)
+        v = torch.randn(k.shape, generator=g, device=dev).to(torch.bfloat16)
+        q = _zero_high_half(torch.randn((B, KVH * G, HD), generator=g, device=dev)).to(torch.bfloat16)
+        nt = B * KVH * (S // 64)
+        if a.workload == "v3":
+            kept = oc.fused_orthocache_attention_v3_gqa(q, k, v, TAU, G)[1]["tiles_retained"]
+            fn = lambda: oc.fused_orthocache_attention_v3_gqa(q, k, v, TAU, G, stats=False)  # noqa: E731
+            nbytes = (nt + kept) * 64 * HD * 2
+        else:
+            norms = oc.tile_high_norms(k.reshape(B * KVH, S, HD)).reshape(B, KVH, S // 64)
+            qn = oc.compute_q_high_norm_exact(q).reshape(B, KVH, G).amax(-1)
+            tau_c = float((qn[..., None] * norms).median()) / (64 * HD)
+            kept = oc.fused_orthocache_attention_cached(q, k, v, norms, tau_c, G)[1]["tiles_retained"]
+            fn = lambda: oc.fused_orthocache_attention_cached(q, k, v, norms, tau_c, G, stats=False)  # noqa: E731
+            nbytes = 2 * kept * 64 * HD * 2 + norms.numel() * 4
+    else:
+        rng = np.random.default_rng(0)
+        lens = rng.integers(2048, 65536 + 1, size=64)
+        lens = (lens - lens % 64).astype(np.int64)[: a.num_seqs]
+        BS = 16
+        nblk = lens // BS
+        total = int(nblk.sum())
+        perm = torch.from_numpy(np.random.default_rng(1).permutation(total).astype(np.int64)).to(dev)
+        kc = torch.empty((total, KVH, BS, HD), dtype=torch.float16, device=dev)
+        vc = torch.empty_like(kc)
+        tables = torch.zeros((len(lens), int(nblk.max())), dtype=torch.int32, device=dev)
+        pos = 0
+        for i in range(len(lens)):
+            nbk = int(nblk[i])
+            pages = perm[pos:pos + nbk]
+            pos += nbk
+            ks = _mixture_device((KVH,), int(lens[i]), HD, g, dev)
+            kc[pages] = ks.reshape(KVH, nbk, BS, HD).permute(1, 0, 2, 3).to(torch.float16)
+            vc[pages] = torch.randn((nbk, KVH, BS, HD), generator=g, device=dev).to(torch.float16)
+            tables[i, :nbk] = pages.to(torch.int32)
+            tables[i, nbk:] = pages[0].to(torch.int32)
+        sl = torch.from_numpy(lens.astype(np.int32)).to(dev)
+        q = _zero_high_half(torch.randn((len(lens), KVH * G, HD), generator=g, device=dev)).to(torch.float16)
+        kept = oc.fused_orthocache_attention_paged(q, kc, vc, tables, None, tau=TAU, seq_lens=sl)[1]["tiles_retained"]
+        fn = lambda: oc.fused_orthocache_attention_paged(q, kc, vc, tables, None, tau=TAU, seq_lens=sl,  # noqa: E731
+                                                         stats=False)
+        nt = int((lens // 64).sum()) * KVH
+        nbytes = (nt + kept) * 64 * HD * 2
+    us = _time_max(fn, False, n=max(1, min(a.steps, 20)), reps=3)
+    print(json.dumps({"workload": a.workload, "num_seqs": a.num_seqs, "launch_us": round(us, 3),
+                      "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "algorithmic_bytes": int(nbytes),
+                      "evict": round(1 - kept / nt, 4)}))
 
 
 def lpt_partition(lengths, world):
@@ -465,6 +531,10 @@ def main():
                 "cpu_baseline": {**vals[0], "value": v},
                 "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
+        return
+
+    if a.quick and a.workload != "v2":
+        quick_workload(a, dev)
         return
 
     import orthocache_gpu_b200 as oc

@@ -110,7 +110,7 @@ bool make_map(CUtensorMap* m, const char* base, int dtype, int hd, bool tc, cons
     last = st * size[r];
     pos[r] = i + 1;
   }
-  cuuint32_t box[4] = {(cuuint32_t)(tc ? 64 : hd), 1, 1, 1};
+  cuuint32_t box[4] = {(cuuint32_t)(tc ? oc::kTcPanel : hd), 1, 1, 1};
   box[pos[0]] = (cuuint32_t)p.box_rows;
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUtensorMapDataType dt;
@@ -121,7 +121,8 @@ bool make_map(CUtensorMap* m, const char* base, int dtype, int hd, bool tc, cons
     default: dt = CU_TENSOR_MAP_DATA_TYPE_UINT8; break;
   }
   const CUresult r = enc(m, dt, 4, const_cast<char*>(base), gdim, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         tc ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                         tc ? (oc::kTcPanel == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)
+                            : CU_TENSOR_MAP_SWIZZLE_NONE,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -184,14 +185,15 @@ int sms_or_device(int num_sms) {
 //   fixed header (kFixedBytes): the per-unit tile prefix for the merge
 //     kernel and the per-team retained-tile counts (both written by every
 //     launch before they are read, so the workspace needs no initialisation)
-//   part  partial states, 2 slots per team of warps: 2*kMaxWarps*gc*(hd+16) f32
+//   part  partial states, 2 slots per team of warps: 2*kMaxTeams*gc*(hd+32) f32
+//         (each of a team's P panels keeps its columns plus m, l and padding)
 constexpr int64_t kMaxUnits = 2048;  // units per launch (shared-memory prefix arrays)
-constexpr int64_t kMaxWarps = 1280;
+constexpr int64_t kMaxTeams = 1280;  // teams of warps per grid (the kernel clamps its grid to this)
 constexpr size_t pad256(size_t b) { return (b + 255) & ~size_t(255); }
 constexpr size_t kFixedBytes = pad256(4 * 4 * kMaxUnits);
 // per-team retained-tile counts live in the second half of the fixed header
 constexpr size_t kTeamKeptOffset = pad256(4 * (kMaxUnits + 1));
-static_assert(kTeamKeptOffset + 4 * kMaxWarps <= kFixedBytes, "fixed workspace header");
+static_assert(kTeamKeptOffset + 4 * kMaxTeams <= kFixedBytes, "fixed workspace header");
 
 struct WsLayout {
   size_t part, total;
@@ -200,7 +202,7 @@ struct WsLayout {
 WsLayout ws_layout(int64_t /*units*/, int gc, int64_t /*num_tiles*/, int hd) {
   WsLayout L;
   L.part = kFixedBytes;
-  L.total = L.part + pad256(4 * (size_t)2 * kMaxWarps * gc * (hd + 16));
+  L.total = L.part + pad256(4 * (size_t)2 * kMaxTeams * gc * (hd + 32));
   return L;
 }
 

@@ -89,6 +89,14 @@ constexpr int kUnrollPairs = OC_UNROLL_PAIRS;
 #define OC_MAX_WARPS_PER_CTA 8
 #endif
 constexpr int kMaxWarpsPerCta = OC_MAX_WARPS_PER_CTA;
+// Width in columns of a warp's panel on the tensor-core path: 64 (128-byte
+// rows, 128-byte TMA swizzle) or 32 (64-byte rows, 64-byte swizzle; twice the
+// warps share a tile).
+#ifndef OC_TC_PANEL
+#define OC_TC_PANEL 64
+#endif
+constexpr int kTcPanel = OC_TC_PANEL;
+static_assert(kTcPanel == 64 || kTcPanel == 32, "tensor-core panel width");
 constexpr int kUnrollPV = OC_UNROLL_PV;
 
 struct DecodeParams {
@@ -326,16 +334,16 @@ struct Cfg {
   static constexpr int LGB = ATTN ? GC * 64 * 4 : 0;
   // Tensor-core path: a team of P = HD/64 warps shares each tile, one
   // 64-column panel (HDL columns) per warp; otherwise P = 1.
-  static constexpr int P = TC ? HD / 64 : 1;
+  static constexpr int P = TC ? HD / kTcPanel : 1;
   static constexpr int HDL = HD / P;
-  static constexpr int SLOT = 64 * ROWMAX / P;  // a multiple of 1024: 128-byte swizzle atoms stay aligned
+  static constexpr int SLOT = 64 * ROWMAX / P;  // a multiple of 1024: swizzle atoms stay aligned
   static constexpr int RING = 208 * 1024;
   static constexpr int NW0 = RING / (NSLOT * (SLOT + LGB));
   static constexpr int NWC = NW0 > kMaxWarpsPerCta ? kMaxWarpsPerCta : NW0;
   static constexpr int NW = NWC < P ? P : NWC / P * P;  // whole teams
   static constexpr int NT = NW * 32;
   static constexpr int MAXU = 2048;  // units per launch (the host batches larger problems)
-  static constexpr int MAXW = 1280;  // warps per grid
+  static constexpr int MAXT = 1280;  // teams per grid (partial-state slots of the workspace)
   static constexpr int OFF_LGS = NW * NSLOT * SLOT;         // logits of slot s: [NW][NSLOT][GC*64] floats
   static constexpr int OFF_BAR = OFF_LGS + NW * NSLOT * LGB;  // full barrier of each slot
   static constexpr int OFF_XCH = OFF_BAR + 8 * NW * NSLOT;    // band energies exchanged in a team: [NW/P][2][P] float2
@@ -509,18 +517,23 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // Per-lane parts of the ldmatrix addresses (x = lane & 7, b3 / b4 = lane bits 3 / 4):
   // every row a lane addresses has (row & 7) == x, so the swizzled chunk of
   // column 16 c + 8 b is ((2 c + b) ^ x).
+  // With 32-column panels rows are 64 bytes and the 64-byte swizzle XORs the
+  // chunk (0..3) with (token >> 1) & 3, which is (x >> 1) & 3 for every row a
+  // lane addresses.
+  constexpr uint32_t kRowB = 2u * HDL;  // bytes of a panel row
+  const uint32_t kSwz = HDL == 64 ? (uint32_t)(lane & 7) : (uint32_t)((lane & 7) >> 1);
   uint32_t ch3[TC ? HDL / 16 : 1], ch4[TC ? HDL / 16 : 1];
   uint32_t offG = 0, offL = 0, offV = 0;
   if constexpr (TC) {
     const uint32_t x = lane & 7, b3 = (lane >> 3) & 1, b4 = (lane >> 4) & 1;
 #pragma unroll
     for (int c2 = 0; c2 < HDL / 16; ++c2) {
-      ch3[c2] = ((2u * c2 + b3) ^ x) << 4;
-      ch4[c2] = ((2u * c2 + b4) ^ x) << 4;
+      ch3[c2] = ((2u * c2 + b3) ^ kSwz) << 4;
+      ch4[c2] = ((2u * c2 + b4) ^ kSwz) << 4;
     }
-    offG = (x + 32u * b4) * 128u;  // gate: tokens 8 s4 + x (+32), columns 16 np + 8 b3
-    offL = (x + 8u * b3) * 128u;   // logits: tokens 16 mt + x + 8 b3, columns 16 ks + 8 b4
-    offV = (x + 8u * b4) * 128u;   // P V: tokens 16 ks + x + 8 b4, columns 16 mt + 8 b3
+    offG = (x + 32u * b4) * kRowB;  // gate: tokens 8 s4 + x (+32), columns 16 np + 8 b3
+    offL = (x + 8u * b3) * kRowB;   // logits: tokens 16 mt + x + 8 b3, columns 16 ks + 8 b4
+    offV = (x + 8u * b4) * kRowB;   // P V: tokens 16 ks + x + 8 b4, columns 16 mt + 8 b3
   }
 
   // TMA copy of tile `tile` of unit u (K or V) into ring slot s: one box per
@@ -550,7 +563,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     if (p.layout == LAYOUT_LINEAR) {  // one box of 64 rows
       if (lane == 0) {
         mbar_arrive_expect_tx(fbar, 64u * row / P);
-        tma_load_4d(dst, tm, panel * 64, crd(1, tile * 64, kvh, seq), crd(2, tile * 64, kvh, seq),
+        tma_load_4d(dst, tm, panel * HDL, crd(1, tile * 64, kvh, seq), crd(2, tile * 64, kvh, seq),
                     crd(3, tile * 64, kvh, seq), fbar, pol);
       }
       return;
@@ -576,7 +589,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
           pb = 0;
         }
         const int tk = t & ((1 << p.block_shift) - 1);
-        tma_load_4d(dst + (uint32_t)(lane * RB * (row / P)), tm, panel * 64, crd(1, tk, kvh, pb),
+        tma_load_4d(dst + (uint32_t)(lane * RB * (row / P)), tm, panel * HDL, crd(1, tk, kvh, pb),
                     crd(2, tk, kvh, pb), crd(3, tk, kvh, pb), fbar, pol);
       }
       return;
@@ -589,7 +602,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         pb = 0;
       }
       const int tk = t & ((1 << p.block_shift) - 1);
-      tma_load_4d(dst + (uint32_t)(run * RB * (row / P)), tm, panel * 64, crd(1, tk, kvh, pb), crd(2, tk, kvh, pb),
+      tma_load_4d(dst + (uint32_t)(run * RB * (row / P)), tm, panel * HDL, crd(1, tk, kvh, pb), crd(2, tk, kvh, pb),
                   crd(3, tk, kvh, pb), fbar, pol);
     }
   };
@@ -642,13 +655,28 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 #pragma unroll 4
     for (int np = 0; np < HDL / 16; ++np) {
       float cl[4] = {}, cd[4][4] = {};
+#ifdef OC_GATE_ILP
+      // low-band partials of the four k-steps in separate accumulators (no
+      // dependent MMA chain), added afterwards
+      float cls[4][4] = {};
 #pragma unroll
       for (int s4 = 0; s4 < 4; ++s4) {
         uint32_t a[4];
-        ldsm_x4_t(base + offG + s4 * 1024 + ch3[np], a);  // tc_addr(8 s4 + x + 32 b4, 16 np + 8 b3)
+        ldsm_x4_t(base + offG + s4 * 8 * kRowB + ch3[np], a);  // tc_addr(8 s4 + x + 32 b4, 16 np + 8 b3)
+        if (need_low) mma16816<KBF16>(cls[s4], a, bLow, bLow);
+        mma16816<KBF16>(cd[s4], a, bDiff, bNeg);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cl[j] = (cls[0][j] + cls[1][j]) + (cls[2][j] + cls[3][j]);
+#else
+#pragma unroll
+      for (int s4 = 0; s4 < 4; ++s4) {
+        uint32_t a[4];
+        ldsm_x4_t(base + offG + s4 * 8 * kRowB + ch3[np], a);  // tc_addr(8 s4 + x + 32 b4, 16 np + 8 b3)
         if (need_low) mma16816<KBF16>(cl, a, bLow, bLow);
         mma16816<KBF16>(cd[s4], a, bDiff, bNeg);
       }
+#endif
       el2 = __ffma2_rn(make_float2(cl[0], cl[1]), make_float2(cl[0], cl[1]), el2);
       el2 = __ffma2_rn(make_float2(cl[2], cl[3]), make_float2(cl[2], cl[3]), el2);
 #pragma unroll
@@ -770,7 +798,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         lq += __shfl_xor_sync(0xffffffffu, lq, 2);
         // one query at a time: the lanes holding its columns stage them in
         // shared memory, then every lane writes two consecutive columns
-        static_assert(!TC || HDL == 64, "tensor-core panels are 64 columns");
+        static_assert(!TC || HDL == 64 || HDL == 32, "tensor-core panels are 64 or 32 columns");
         const float2* stg2 = reinterpret_cast<const float2*>(stg);
 #pragma unroll
         for (int q = 0; q < GC; ++q) {
@@ -784,10 +812,12 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
             }
             __syncwarp();
           }
-          const float2 v = empty ? make_float2(0.f, 0.f) : stg2[lane];
+          const float2 v = (empty || 2 * lane >= HDL) ? make_float2(0.f, 0.f) : stg2[lane];
           const float mq = __shfl_sync(0xffffffffu, m_mine, 4 * q), lqq = __shfl_sync(0xffffffffu, lq, 4 * q);
-          put(q, 2 * lane, mq, lqq, v.x);
-          put(q, 2 * lane + 1, mq, lqq, v.y);
+          if (2 * lane < HDL) {
+            put(q, 2 * lane, mq, lqq, v.x);
+            put(q, 2 * lane + 1, mq, lqq, v.y);
+          }
           __syncwarp();
         }
         if (!direct && t4 == 0 && g8 < GC)
@@ -1138,7 +1168,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 #pragma unroll
               for (int mt = 0; mt < 4; ++mt) {
                 uint32_t a4[4];
-                ldsm_x4(base + offL + mt * 2048 + ch4[ks], a4);  // tc_addr(16 mt + x + 8 b3, 16 ks + 8 b4)
+                ldsm_x4(base + offL + mt * 16 * kRowB + ch4[ks], a4);  // tc_addr(16 mt + x + 8 b3, 16 ks + 8 b4)
                 mma16816<KBF16>(cq[mt], a4, qf[ks][0], qf[ks][1]);
               }
             // C(token, query): lane holds tokens 16mt+g8 (+8), queries 2t4, 2t4+1
@@ -1285,7 +1315,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 #pragma unroll
           for (int mt = 0; mt < HDL / 16; ++mt) {
             uint32_t a4[4];
-            ldsm_x4_t(base + offV + ks * 2048 + ch3[mt], a4);  // tc_addr(16 ks + x + 8 b4, 16 mt + 8 b3)
+            ldsm_x4_t(base + offV + ks * 16 * kRowB + ch3[mt], a4);  // tc_addr(16 ks + x + 8 b4, 16 mt + 8 b3)
             mma16816<KBF16>(tacc[mt], a4, bh[ks][0], bh[ks][1]);
             if constexpr (!PACK) mma16816<KBF16>(tacc[mt], a4, bl[ks][0], bl[ks][1]);
           }
@@ -1491,7 +1521,7 @@ cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tk, const CU
   const int sms_cap = (num_sms > 0 && num_sms < dev_sms[dev]) ? num_sms : dev_sms[dev];
   const int64_t cap = (int64_t)sms_cap * resident[dev];
   int64_t grid = want < 1 ? 1 : (want > cap ? cap : want);
-  if (grid * CF::NW > CF::MAXW) grid = CF::MAXW / CF::NW;
+  if (grid * (CF::NW / CF::P) > CF::MAXT) grid = CF::MAXT / (CF::NW / CF::P);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(CF::NT);
