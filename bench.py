@@ -639,6 +639,15 @@ def main():
                    "gbs": round(nb / (gus * 1e-6) / 1e9, 1), "evict": round(1 - kp / (HEADS * sl // 64), 3)}
             row.update({kk_: round(vv_, 2) if isinstance(vv_, float) else vv_
                         for kk_, vv_ in dense_decode_us(qs, ks, vs).items()})
+            # the cached-norm gate on the same heads (norms scored once, as at prefill):
+            # evicted tiles cost neither K nor V; tau at the median bound
+            nrm = oc.tile_high_norms(ks)
+            qn = oc.compute_q_high_norm_exact(qs)
+            tc_ = float((qn[:, None] * nrm).median()) / (64 * HEAD_DIM)
+            g2 = graph_of(lambda i=0: oc.fused_orthocache_attention_cached(qs, ks, vs, nrm, tc_, 1, stats=False), 50)
+            row["cached_gate_us_graph"] = round(time_fn(g2.replay, 10) / 50, 2)
+            row["cached_gate_evict"] = round(oc.fused_orthocache_attention_cached(qs, ks, vs, nrm, tc_, 1)[1]
+                                             ["eviction_rate"], 3)
             sweep.append(row)
             if sl != seq:
                 del qs, ks, vs
