@@ -453,6 +453,9 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   mbar_init_fence();
   __syncwarp();
 
+  // LIST mode: the lists come from the gate kernel, launched just before as
+  // this grid's programmatic predecessor; everything above overlapped it
+  if (p.list_count != nullptr) asm volatile("griddepcontrol.wait;" ::: "memory");
   // ---- tiles per unit, prefix in shared memory
   for (int u = tid; u < U; u += blockDim.x) {
     int T = p.num_tiles;
@@ -1527,7 +1530,11 @@ cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tk, const CU
   cfg.blockDim = dim3(CF::NT);
   cfg.dynamicSmemBytes = CF::SMEM;
   cfg.stream = stream;
-  cfg.numAttrs = 0;
+  cudaLaunchAttribute da[1];
+  da[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  da[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = da;
+  cfg.numAttrs = p.list_count != nullptr ? 1 : 0;  // LIST mode follows its gate kernel
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
   if (e != cudaSuccess || !ATTN) return e;
   // merge of the units shared by several teams: a programmatic dependent launch

@@ -121,6 +121,9 @@ __global__ void __launch_bounds__(256) decode_gate_kernel(
   __shared__ float qn[64];
   __shared__ float s_stat;
   __shared__ int wsum[8];
+  // the decode grid that consumes the lists may start its prologue now; its
+  // griddepcontrol.wait still waits for this grid to complete
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int seq = blockIdx.x / num_kv_heads, kvh = blockIdx.x % num_kv_heads;
   const int g_idx = blockIdx.x;  // (seq, kv head) row of the outputs
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
