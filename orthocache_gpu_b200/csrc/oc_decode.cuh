@@ -926,7 +926,21 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   tr_b = oc_clock();
 #endif
   if (fb > fa) enter_unit(u_first, fa);
+  // LIST mode: every tile is retained, so a tile's V copy is issued into the
+  // slot right after its K copy (both in flight at once); the V item reads
+  // the logits its K item left in the preceding slot's logit area.
+  const bool paired = ATTN && p.tile_list != nullptr;
+  int pend_v = 0, pv_seq = 0, pv_kvh = 0, pv_tile = 0, pv_da = 0, pv_u = 0;
   auto issue_next = [&](uint32_t s) {
+    if (paired && pend_v) {
+      issue(s, pv_seq, pv_kvh, pv_tile, true);
+      if (lane == (int)s) {
+        dsc_a = pv_da | 1;
+        dsc_b = (pv_u << 20) | pv_tile;
+      }
+      pend_v = 0;
+      return;
+    }
     if (f_iss < fb) {
       if (f_iss >= u_end_iss) {
         int u = u_iss + 1;
@@ -938,6 +952,14 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       if (lane == (int)s) {
         dsc_a = 2 * (int)(f_iss - fa);
         dsc_b = (u_iss << 20) | tile;
+      }
+      if (paired) {
+        pend_v = 1;
+        pv_seq = seq_iss;
+        pv_kvh = kvh_iss;
+        pv_tile = tile;
+        pv_da = 2 * (int)(f_iss - fa);
+        pv_u = u_iss;
       }
       it_iss.next();
       ++f_iss;
@@ -974,7 +996,8 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     if (tr_t2 == 0) tr_t2 = oc_clock();
     if (isv) ++tr_nv; else ++tr_nk;
 #endif
-    float* lgs = lgs_base + s * (CF::LGB / 4);
+    const uint32_t ls = (paired && isv) ? (s + NSLOT - 1) % NSLOT : s;  // slot holding this tile's logits
+    float* lgs = lgs_base + ls * (CF::LGB / 4);
     if (!isv) {
       // ================================================ K tile: gate (+ logits)
       if (u != u_k) {
@@ -1210,10 +1233,12 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
               *reinterpret_cast<float2*>(dstl + g * 64 + rg * RPL + m) = make_float2(lg[h], lg[h + 1]);
             }
           }
-          __syncwarp();  // K tile read, logits stored: the slot takes this tile's V
-          issue(s, seq_k, kvh_k, tile, true);
-          if (lane == (int)s) dsc_a |= 1;
-          v_issued = true;
+          if (!paired) {
+            __syncwarp();  // K tile read, logits stored: the slot takes this tile's V
+            issue(s, seq_k, kvh_k, tile, true);
+            if (lane == (int)s) dsc_a |= 1;
+            v_issued = true;
+          }
         }
       }
       if (!v_issued) {
@@ -1248,7 +1273,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
             float2 t = make_float2(0.f, 0.f);
 #pragma unroll
             for (int q = 0; q < P; ++q) {
-              const float2 v = *reinterpret_cast<const float2*>(lgs_all + ((team * P + q) * NSLOT + s) * (CF::LGB / 4) + o);
+              const float2 v = *reinterpret_cast<const float2*>(lgs_all + ((team * P + q) * NSLOT + ls) * (CF::LGB / 4) + o);
               t.x += v.x;
               t.y += v.y;
             }
