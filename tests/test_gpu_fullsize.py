@@ -213,3 +213,38 @@ def test_long_context_512k_sharded_decode():
     assert 0.4 < gm["eviction_rate"] < 0.6
     for w, e in err.items():
         assert e <= 2e-3, f"512K, {w} shard(s): max abs error {e:.3g}"
+
+
+def test_cached_gate_decode_config3_full_size():
+    # the O(1) cached-norm gate at the V3 shapes: norms scored once on the GPU
+    # (band [48, 64)), tau between two neighbouring bounds at the median
+    B, KVH, G, S, HD, dt = 16, 8, 4, 32768, 128, torch.bfloat16
+    k = torch.empty((B, KVH, S, HD), dtype=dt, device=DEV)
+    v = torch.empty_like(k)
+    for b in range(B):
+        for h, (kh, vh) in enumerate(_heads(3000 + b, KVH, S, HD, dt)):
+            k[b, h] = torch.from_numpy(kh).to(dt)
+            v[b, h] = torch.from_numpy(vh).to(dt)
+    qn = _rt(zero_high_band_queries(np.random.default_rng(78).standard_normal((B, KVH * G, HD), dtype=np.float32)), dt)
+    q = torch.from_numpy(qn).to(dt).to(DEV)
+    norms = oc.tile_high_norms(k.reshape(B * KVH, S, HD)).reshape(B, KVH, S // 64)
+    nrm = as_np(norms)
+    bounds = np.sort(np.concatenate([orc.decode_gate(qn[b], nrm[b], 1.0, S // 64, G)[2].ravel() for b in range(B)]))
+    i = len(bounds) // 2
+    while bounds[i + 1] - bounds[i] < 1e-3 * bounds[i]:
+        i += 1
+    tau = float((bounds[i] + bounds[i + 1]) / 2) / (64 * HD)
+    out, meta = oc.fused_orthocache_attention_cached(q, k, v, norms, tau, G, return_mask=True)
+    out = as_np(out)
+    ev_gpu = as_np(meta["evict_mask"]).astype(bool)
+    kept, err = 0, 0.0
+    for b in range(B):
+        heads = list(_heads(3000 + b, KVH, S, HD, dt))
+        kh = np.stack([a for a, _ in heads])
+        np.testing.assert_allclose(nrm[b], orc.tile_high_norms(kh), rtol=1e-5)
+        ref, ev, bound = orc.cached_attention(qn[b], kh, np.stack([c for _, c in heads]), nrm[b], tau, G)
+        assert_mask(~ev_gpu[b], ~ev, bound, tau * 64 * HD, f"cached seq {b}")
+        kept += int((~ev).sum())
+        err = max(err, float(np.abs(out[b] - ref).max()))
+    assert meta["tiles_retained"] == kept and 0.4 < meta["eviction_rate"] < 0.6
+    assert err <= 2e-3, f"cached decode: max abs error {err:.3g}"
