@@ -929,7 +929,10 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // LIST mode: every tile is retained, so a tile's V copy is issued into the
   // slot right after its K copy (both in flight at once); the V item reads
   // the logits its K item left in the preceding slot's logit area.
-  const bool paired = ATTN && p.tile_list != nullptr;
+#ifndef OC_LIST_PAIRED
+#define OC_LIST_PAIRED 0  // measured slower (192 vs 209 us at the V3 shapes); kept as a build option
+#endif
+  const bool paired = OC_LIST_PAIRED && ATTN && p.tile_list != nullptr;
   int pend_v = 0, pv_seq = 0, pv_kvh = 0, pv_tile = 0, pv_da = 0, pv_u = 0;
   auto issue_next = [&](uint32_t s) {
     if (paired && pend_v) {
