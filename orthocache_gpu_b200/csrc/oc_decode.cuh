@@ -414,7 +414,13 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   const unsigned long long tr_t0 = oc_clock();
   unsigned long long tr_t1 = 0, tr_t2 = 0, tr_a = 0, tr_b = 0, tr_x[4] = {0, 0, 0, 0};
   int tr_nk = 0, tr_nv = 0;
-  unsigned long long tr_wait = 0, tr_sync = 0;
+  unsigned long long tr_wait = 0, tr_sync = 0, tr_polls = 0;
+  long long tr_sec[6] = {0, 0, 0, 0, 0, 0};  // SM cycles: gate, logits, V step, issue, finalize, loop
+#define OC_TR_BEGIN(v) const long long v = clock64()
+#define OC_TR_END(i, v) tr_sec[i] += clock64() - (v)
+#else
+#define OC_TR_BEGIN(v)
+#define OC_TR_END(i, v)
 #endif
   const int c = lane % C, rg = lane / C;
   static_assert(!TC || (CF::KB == 2 && CF::VB == 2 && HD >= 64 && GC <= 8), "tensor-core path");
@@ -616,8 +622,17 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 #ifdef OC_TRACE
     const unsigned long long c0 = oc_clock();
 #endif
+#ifdef OC_TRACE
+    {
+      uint32_t i = 0;
+      while (i < kWaitLimit && !mbar_try_wait(bar0 + 8u * s, (phases >> s) & 1u)) ++i;
+      tr_polls += i + 1;
+      if (i == kWaitLimit && lane == 0) atomicOr(p.status, ST_TIMEOUT);
+    }
+#else
     if (!mbar_wait_bounded(bar0 + 8u * s, (phases >> s) & 1u, kWaitLimit) && lane == 0)
       atomicOr(p.status, ST_TIMEOUT);
+#endif
 #ifdef OC_TRACE
     tr_wait += oc_clock() - c0;
 #endif
@@ -1083,7 +1098,9 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       float score = 0.f;
       if (p.gate != GATE_LIST) {
       if constexpr (TC) {
+        OC_TR_BEGIN(tg0);
         score = tc_gate(ts);
+        OC_TR_END(0, tg0);
       } else {
         float2 sres[NRES][D2];
         float2 ehd[D2];  // one E_high accumulator per column pair: independent FMA chains
@@ -1187,6 +1204,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         if (chunk_k == 0 && panel == 0) ++kept_stat;
         if constexpr (ATTN) {
           ++kept_k;
+          OC_TR_BEGIN(tl0);
           if constexpr (TC) {
             // logits = K (tokens x dims) * q (dims x queries): 4 token tiles of
             // 16, over this warp's panel (the team adds the panels' partials)
@@ -1236,17 +1254,22 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
               *reinterpret_cast<float2*>(dstl + g * 64 + rg * RPL + m) = make_float2(lg[h], lg[h + 1]);
             }
           }
+          OC_TR_END(1, tl0);
           if (!paired) {
+            OC_TR_BEGIN(ti0);
             __syncwarp();  // K tile read, logits stored: the slot takes this tile's V
             issue(s, seq_k, kvh_k, tile, true);
+            OC_TR_END(3, ti0);
             if (lane == (int)s) dsc_a |= 1;
             v_issued = true;
           }
         }
       }
       if (!v_issued) {
+        OC_TR_BEGIN(ti1);
         __syncwarp();
         issue_next(s);
+        OC_TR_END(3, ti1);
       }
       if constexpr (ATTN) {
         const int uend = uend_k;
@@ -1254,6 +1277,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       }
     } else {
       // ================================================ V tile of a retained tile
+      OC_TR_BEGIN(tv0);
       if (acc_unit != u) {
         acc_unit = u;
         ua_acc = tp[u];
@@ -1384,9 +1408,13 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
           }
         }
       }
+      OC_TR_END(2, tv0);
+      OC_TR_BEGIN(ti2);
       __syncwarp();
       issue_next(s);
+      OC_TR_END(3, ti2);
     }
+    OC_TR_BEGIN(tf0);
     if constexpr (ATTN) {
       if (acc_unit >= 0) {
         const int ua = ua_acc, uend = uend_acc;
@@ -1399,6 +1427,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
         }
       }
     }
+    OC_TR_END(4, tf0);
   }
   if constexpr (ATTN) {
     // every team of the grid writes its count (no zeroing needed); merge_kernel sums them
@@ -1410,11 +1439,12 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // griddepcontrol.wait still waits for the whole grid to complete)
 #ifdef OC_TRACE
   if (p.trace != nullptr && panel == 0 && lane == 0) {
-    unsigned long long* r = p.trace + 16 * wg;
+    unsigned long long* r = p.trace + 24 * wg;
     r[0] = tr_t0; r[1] = tr_t1; r[2] = tr_t2; r[3] = oc_clock();
     r[4] = tr_a; r[5] = tr_b; r[6] = tr_nk; r[7] = tr_nv;
     for (int i = 0; i < 4; ++i) r[8 + i] = tr_x[i];
-    r[12] = tr_wait; r[13] = tr_sync;
+    r[12] = tr_wait; r[13] = tr_sync; r[14] = tr_polls;
+    for (int i = 0; i < 6; ++i) r[16 + i] = (unsigned long long)tr_sec[i];
   }
 #endif
   if constexpr (ATTN) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1435,8 +1465,8 @@ __global__ void __launch_bounds__(128) merge_kernel(const DecodeParams p, int64_
   asm volatile("griddepcontrol.wait;" ::: "memory");
 #ifdef OC_TRACE
   if (p.trace != nullptr && threadIdx.x == 0) {
-    p.trace[16 * W + 3 * blockIdx.x] = tr_m0;
-    p.trace[16 * W + 3 * blockIdx.x + 1] = oc_clock();
+    p.trace[24 * W + 3 * blockIdx.x] = tr_m0;
+    p.trace[24 * W + 3 * blockIdx.x + 1] = oc_clock();
   }
 #endif
   const int lane = threadIdx.x & 31;
