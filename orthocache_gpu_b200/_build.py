@@ -89,6 +89,31 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None, o
     return lib_path
 
 
+BINDING = os.path.join(OUT_DIR, "oc_torch.so")
+
+
+def build_binding(force: bool = False, verbose: bool = False) -> str:
+    """Compile the pybind11 binding csrc/oc_torch.cpp (C++, no GPU code) into _lib/oc_torch.so.
+
+    It links liborthocache_b200.so from the same directory (rpath $ORIGIN).
+    """
+    src = os.path.join(CSRC, "oc_torch.cpp")
+    deps = [src, LIB, os.path.join(ROOT, "include", "orthocache_b200.h")]
+    if not force and os.path.exists(BINDING) and all(os.path.getmtime(d) <= os.path.getmtime(BINDING) for d in deps):
+        return BINDING
+    from torch.utils import cpp_extension
+    tmp = os.path.join(OUT_DIR, "oc_torch_build")
+    os.makedirs(tmp, exist_ok=True)
+    cpp_extension.load(name="oc_torch", sources=[src], build_directory=tmp, verbose=verbose,
+                       extra_cflags=["-O2"], extra_ldflags=[f"-L{OUT_DIR}", "-lorthocache_b200",
+                                                           "'-Wl,-rpath,$$ORIGIN:$$ORIGIN/..'"],
+                       is_python_module=True)
+    shutil.copy2(os.path.join(tmp, "oc_torch.so"), BINDING + ".tmp")
+    os.replace(BINDING + ".tmp", BINDING)
+    return BINDING
+
+
 if __name__ == "__main__":
     import sys
     print(build(force="--force" in sys.argv, verbose=True))
+    print(build_binding(force="--force" in sys.argv))

@@ -84,6 +84,31 @@ def load() -> C.CDLL:
     return _lib
 
 
+_binding = None
+_binding_tried = False
+
+
+def binding():
+    """The compiled binding (_lib/oc_torch.so) of the hot calls, or None.
+
+    It calls the same C ABI with less host overhead per call than ctypes.
+    Not used when ORTHOCACHE_B200_LIB selects another build of the library
+    (the binding links the in-tree one).
+    """
+    global _binding, _binding_tried
+    if not _binding_tried:
+        _binding_tried = True
+        path = os.path.join(_PKG, "_lib", "oc_torch.so")
+        if not os.environ.get("ORTHOCACHE_B200_LIB") and os.path.exists(path):
+            import importlib.util
+            load()
+            spec = importlib.util.spec_from_file_location("oc_torch", path)
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            _binding = mod
+    return _binding
+
+
 def dtype_code(t: torch.Tensor) -> int:
     try:
         return _DTYPE[t.dtype]

@@ -97,21 +97,18 @@ def fused_orthocache_attention_v2(
     keys, values = _lib.harmonize_kv(keys, values)
     keys = _lib.prepare_kv(keys)
     values = _lib.prepare_kv(values)
-    out = torch.empty((num_heads, head_dim), dtype=input_dtype, device=dev)
     mask = torch.empty((num_heads, num_tiles), dtype=torch.bool, device=dev) if return_mask else None
 
     stream = _lib.stream_ptr(dev)
     ws = _lib.workspace(dev, stream)
     wptr, wbytes = ws.get(_lib.workspace_bytes(num_heads, 1, num_tiles, head_dim))
-    _lib.check(_lib.load().oc_fused_attention_v2(
-        q.data_ptr(), _lib.dtype_code(q), q.stride(0),
-        keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1),
-        values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1),
-        num_heads, seq_len, head_dim, float(zeta_max), num_splits, _lib.num_sms(dev),
-        out.data_ptr(), _lib.dtype_code(out), out.stride(0),
-        _lib.ptr(mask), ws.retained_ptr if stats else 0, ws.status_ptr,
-        wptr, wbytes, stream), "fused_orthocache_attention_v2")
-
+    fast = _lib.binding()
+    if fast is not None:
+        out = fast.v2(q, keys, values, float(zeta_max), num_splits, _lib.num_sms(dev), input_dtype, mask,
+                      ws.retained_ptr if stats else 0, ws.status_ptr, wptr, wbytes, stream)
+    else:
+        out = _v2_ctypes(q, keys, values, zeta_max, num_splits, dev, input_dtype, mask, ws, stats, wptr, wbytes,
+                         stream)
     meta: Dict[str, Any] = {
         "num_splits": num_splits,
         "num_tiles": num_tiles,
@@ -121,6 +118,22 @@ def fused_orthocache_attention_v2(
     if return_mask:
         meta["eviction_mask"] = mask
     return out, _finish_meta(meta, ws, num_tiles * num_heads, stats)
+
+
+def _v2_ctypes(q, keys, values, zeta_max, num_splits, dev, input_dtype, mask, ws, stats, wptr, wbytes, stream):
+    """The V2 launch through ctypes (when the compiled binding is not in use)."""
+    num_heads, head_dim = q.shape[0], q.shape[-1]
+    seq_len = keys.shape[1]
+    out = torch.empty((num_heads, head_dim), dtype=input_dtype, device=dev)
+    _lib.check(_lib.load().oc_fused_attention_v2(
+        q.data_ptr(), _lib.dtype_code(q), q.stride(0),
+        keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1),
+        values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1),
+        num_heads, seq_len, head_dim, float(zeta_max), num_splits, _lib.num_sms(dev),
+        out.data_ptr(), _lib.dtype_code(out), out.stride(0),
+        _lib.ptr(mask), ws.retained_ptr if stats else 0, ws.status_ptr,
+        wptr, wbytes, stream), "fused_orthocache_attention_v2")
+    return out
 
 
 def fused_orthocache_attention(

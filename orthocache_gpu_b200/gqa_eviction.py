@@ -78,20 +78,25 @@ def fused_orthocache_attention_v3_gqa(
     keys, values = _lib.harmonize_kv(keys, values)
     keys = _lib.prepare_kv(keys)
     values = _lib.prepare_kv(values)
-    out = torch.empty((num_seqs, num_query_heads, head_dim), dtype=input_dtype, device=dev)
     mask = torch.empty((num_seqs, num_kv_heads, num_tiles), dtype=torch.bool, device=dev) if return_mask else None
 
     stream = _lib.stream_ptr(dev)
     ws = _lib.workspace(dev, stream)
     wptr, wbytes = ws.get(_lib.workspace_bytes(num_seqs * num_kv_heads, G, num_tiles, head_dim))
-    _lib.check(_lib.load().oc_fused_attention_v3_gqa(
-        q.data_ptr(), _lib.dtype_code(q), q.stride(0), q.stride(1),
-        keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1), keys.stride(2),
-        values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1), values.stride(2),
-        num_seqs, num_kv_heads, G, seq_len, head_dim, float(tau), num_splits, _lib.num_sms(dev),
-        out.data_ptr(), _lib.dtype_code(out), out.stride(0), out.stride(1),
-        _lib.ptr(mask), ws.retained_ptr if stats else 0, ws.status_ptr,
-        wptr, wbytes, stream), "fused_orthocache_attention_v3_gqa")
+    fast = _lib.binding()
+    if fast is not None:
+        out = fast.v3(q, keys, values, float(tau), G, num_splits, _lib.num_sms(dev), input_dtype, mask,
+                      ws.retained_ptr if stats else 0, ws.status_ptr, wptr, wbytes, stream)
+    else:
+        out = torch.empty((num_seqs, num_query_heads, head_dim), dtype=input_dtype, device=dev)
+        _lib.check(_lib.load().oc_fused_attention_v3_gqa(
+            q.data_ptr(), _lib.dtype_code(q), q.stride(0), q.stride(1),
+            keys.data_ptr(), _lib.dtype_code(keys), keys.stride(0), keys.stride(1), keys.stride(2),
+            values.data_ptr(), _lib.dtype_code(values), values.stride(0), values.stride(1), values.stride(2),
+            num_seqs, num_kv_heads, G, seq_len, head_dim, float(tau), num_splits, _lib.num_sms(dev),
+            out.data_ptr(), _lib.dtype_code(out), out.stride(0), out.stride(1),
+            _lib.ptr(mask), ws.retained_ptr if stats else 0, ws.status_ptr,
+            wptr, wbytes, stream), "fused_orthocache_attention_v3_gqa")
 
     if not batched:
         out = out[0]

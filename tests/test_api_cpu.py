@@ -121,3 +121,10 @@ def test_pipeline_dense_mode_and_compact_crossover_bypass_run_on_cpu():
     assert "crossover=512" in meta2["crossover_reason"]
     with pytest.raises(ValueError, match="Unknown mode"):
         oc.orthocache_forward(q, _t(1024, 4, 64), _t(1024, 4, 64), mode="bogus")
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(_lib.LIB_PATH), "oc_torch.so")),
+                    reason="binding not built")
+def test_compiled_binding_loads_and_exports_the_hot_calls():
+    b = _lib.binding()
+    assert b is not None and hasattr(b, "v2") and hasattr(b, "v3")
