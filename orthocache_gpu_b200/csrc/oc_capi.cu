@@ -129,6 +129,58 @@ bool make_map(CUtensorMap* m, const char* base, int dtype, int hd, bool tc, cons
 
 unsigned long long* g_trace = nullptr;  // diagnostics buffer (oc_debug_set_trace)
 
+// Encoded tensor maps are pure functions of their inputs; decode calls repeat
+// them (same cache, same shapes), so each host thread keeps the last few.
+struct MapKey {
+  const char* base;
+  int dtype, hd, tc, isv, layout, box_rows, block_shift, num_kv_heads, num_seqs, num_blocks, num_tiles;
+  int64_t s_tok, s_head, s_outer;
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  int pos[3];
+  bool used;
+};
+
+bool cached_map(CUtensorMap* m, const char* base, int dtype, int hd, bool tc, const DecodeParams& p, bool isv,
+                int (&pos)[3]) {
+  thread_local MapEntry cache[8] = {};
+  thread_local unsigned next = 0;
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));  // padding bytes take part in the comparison
+  k.base = base;
+  k.dtype = dtype;
+  k.hd = hd;
+  k.tc = tc;
+  k.isv = isv;
+  k.layout = p.layout;
+  k.box_rows = p.box_rows;
+  k.block_shift = p.block_shift;
+  k.num_kv_heads = p.num_kv_heads;
+  k.num_seqs = p.num_seqs;
+  k.num_blocks = p.num_blocks;
+  k.num_tiles = p.num_tiles;
+  k.s_tok = isv ? p.v_tok_stride : p.k_tok_stride;
+  k.s_head = isv ? p.v_head_stride : p.k_head_stride;
+  k.s_outer = p.layout == oc::LAYOUT_LINEAR ? (isv ? p.v_seq_stride : p.k_seq_stride)
+                                            : (isv ? p.v_blk_stride : p.k_blk_stride);
+  for (auto& e : cache)
+    if (e.used && e.key == k) {
+      *m = e.map;
+      for (int i = 0; i < 3; ++i) pos[i] = e.pos[i];
+      return true;
+    }
+  if (!make_map(m, base, dtype, hd, tc, p, isv, pos)) return false;
+  MapEntry& e = cache[next++ % 8];
+  e.key = k;
+  e.map = *m;
+  for (int i = 0; i < 3; ++i) e.pos[i] = pos[i];
+  e.used = true;
+  return true;
+}
+
 int run(const DecodeParams& p0, int k_dtype, int v_dtype, int hd, bool attn, int sms, cudaStream_t st) {
   DecodeParams p = p0;
   p.trace = g_trace;
@@ -149,8 +201,8 @@ int run(const DecodeParams& p0, int k_dtype, int v_dtype, int hd, bool attn, int
   std::memset(&maps, 0, sizeof(maps));
   const bool any_tile = p.num_tiles > 0 && p.k != nullptr;
   if (any_tile) {
-    if (!make_map(&maps.k, p.k, k_dtype, hd, tc, p, false, p.tm_pos_k)) return OC_ERR_INVALID;
-    if (attn && !make_map(&maps.v, p.v, v_dtype, hd, tc, p, true, p.tm_pos_v)) return OC_ERR_INVALID;
+    if (!cached_map(&maps.k, p.k, k_dtype, hd, tc, p, false, p.tm_pos_k)) return OC_ERR_INVALID;
+    if (attn && !cached_map(&maps.v, p.v, v_dtype, hd, tc, p, true, p.tm_pos_v)) return OC_ERR_INVALID;
   } else {
     for (int i = 0; i < 3; ++i) p.tm_pos_k[i] = p.tm_pos_v[i] = i + 1;
   }

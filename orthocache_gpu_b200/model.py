@@ -45,14 +45,18 @@ def _rms(x, w, eps):
     return (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
 
 
-def _rope(x, pos, theta):
-    """Rotary embedding (rotate-half form) of x (..., T, hd) at positions pos (T,)."""
-    hd = x.shape[-1]
-    inv = theta ** (-torch.arange(0, hd, 2, device=x.device, dtype=torch.float32) / hd)
+def _rope_tables(max_len, hd, theta, device):
+    """cos / sin tables (max_len, hd) of the rotate-half rotary embedding (same values as _rope)."""
+    pos = torch.arange(max_len, device=device)
+    inv = theta ** (-torch.arange(0, hd, 2, device=device, dtype=torch.float32) / hd)
     ang = pos.float()[:, None] * inv[None, :]
-    cos, sin = torch.cat([ang.cos(), ang.cos()], -1), torch.cat([ang.sin(), ang.sin()], -1)
-    x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
-    rot = torch.cat([-x2, x1], -1)
+    return torch.cat([ang.cos(), ang.cos()], -1), torch.cat([ang.sin(), ang.sin()], -1)
+
+
+def _rope_t(x, cos, sin):
+    """Rotary embedding of x (..., T, hd) with the table rows of its positions."""
+    hd = x.shape[-1]
+    rot = torch.cat([-x[..., hd // 2:], x[..., : hd // 2]], -1)
     return (x.float() * cos + rot.float() * sin).to(x.dtype)
 
 
@@ -89,6 +93,7 @@ class GatedLlama:
         self.k_cache = [torch.zeros(max_len, s.kv_heads, s.head_dim, device=self.dev, dtype=dtype)
                         for _ in range(s.layers)]
         self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
+        self._cos, self._sin = _rope_tables(max_len, s.head_dim, s.rope_theta, self.dev)
         self.length = 0
         self.tau: List[Optional[float]] = [None] * s.layers
         self.kept = 0
@@ -106,7 +111,8 @@ class GatedLlama:
         q = (h @ L["wq"]).view(T, s.heads, s.head_dim).transpose(0, 1)
         k = (h @ L["wk"]).view(T, s.kv_heads, s.head_dim).transpose(0, 1)
         v = (h @ L["wv"]).view(T, s.kv_heads, s.head_dim).transpose(0, 1)
-        return _rope(q, pos, s.rope_theta), _rope(k, pos, s.rope_theta), v
+        cos, sin = self._cos.index_select(0, pos), self._sin.index_select(0, pos)   # (T, hd) tables
+        return _rope_t(q, cos, sin), _rope_t(k, cos, sin), v
 
     def _mlp(self, L, x):
         h = _rms(x, L["ln2"], self.s.eps)
