@@ -262,6 +262,8 @@ def prepare_kv(t: torch.Tensor) -> torch.Tensor:
     Copies only when the given layout cannot be streamed directly.
     """
     es = t.element_size()
+    if t.is_contiguous() and (t.shape[-1] * es) % 16 == 0 and t.data_ptr() % 16 == 0:
+        return t  # the common case, checked without walking the strides in Python
     ok = t.stride(-1) == 1 and t.data_ptr() % 16 == 0 and all((s * es) % 16 == 0 for s in t.stride()[:-1])
     if ok:
         return t
