@@ -941,6 +941,9 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   tr_b = oc_clock();
 #endif
   if (fb > fa) enter_unit(u_first, fa);
+#ifdef OC_TRACE
+  unsigned long long tr_c = oc_clock(), tr_d = 0;
+#endif
   // LIST mode: every tile is retained, so a tile's V copy is issued into the
   // slot right after its K copy (both in flight at once); the V item reads
   // the logits its K item left in the preceding slot's logit area.
@@ -986,7 +989,12 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
       dsc_a = -1;
     }
   };
-  for (uint32_t s = 0; s < NSLOT; ++s) issue_next(s);
+  for (uint32_t s = 0; s < NSLOT; ++s) {
+    issue_next(s);
+#ifdef OC_TRACE
+    if (s == 0) tr_d = oc_clock();
+#endif
+  }
 #ifdef OC_TRACE
   tr_t1 = oc_clock();
 #endif
@@ -1445,6 +1453,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     for (int i = 0; i < 4; ++i) r[8 + i] = tr_x[i];
     r[12] = tr_wait; r[13] = tr_sync; r[14] = tr_polls;
     for (int i = 0; i < 6; ++i) r[16 + i] = (unsigned long long)tr_sec[i];
+    r[22] = tr_c; r[23] = tr_d;
   }
 #endif
   if constexpr (ATTN) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
