@@ -1462,12 +1462,16 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 // Merge of the units that several teams share, launched as a programmatic
 // dependent of decode_kernel: griddepcontrol.wait returns once the decode
 // grid has completed and its stores are visible, so the partial states need
-// no fences or tickets.  One warp per (unit, 64-column panel) combines the
-// unit's partial states (log-sum-exp: running max M, weights 2^(m - M)) and
-// writes the output; units held whole by one team were written directly.
+// no fences or tickets.  One CTA per (unit, 64-column panel, query head of
+// the chunk): its kMergeWarps warps each combine a contiguous share of the
+// unit's partial states (log-sum-exp: running max M, weights 2^(m - M)), and
+// warp 0 combines the warps' states through shared memory and writes the
+// output.  Units held whole by one team were written directly.
+constexpr int kMergeWarps = 4;
+
 template <int HD, int GC, int P>
-__global__ void __launch_bounds__(128) merge_kernel(const DecodeParams p, int64_t W) {
-  constexpr int HDL = HD / P, PST = HDL + 4;
+__global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(const DecodeParams p, int64_t W) {
+  constexpr int HDL = HD / P, PST = HDL + 4, MW = kMergeWarps;
 #ifdef OC_TRACE
   const unsigned long long tr_m0 = oc_clock();
 #endif
@@ -1478,11 +1482,10 @@ __global__ void __launch_bounds__(128) merge_kernel(const DecodeParams p, int64_
     p.trace[24 * W + 3 * blockIdx.x + 1] = oc_clock();
   }
 #endif
-  const int lane = threadIdx.x & 31;
-  const int64_t item = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nchunks = (p.group + GC - 1) / GC;
   const int U = p.num_seqs * p.num_kv_heads * nchunks;
-  if (p.stats != nullptr && blockIdx.x == 0 && threadIdx.x < 32) {  // retained-tile count of the launch
+  if (p.stats != nullptr && blockIdx.x == 0 && wid == 0) {  // retained-tile count of the launch
     int s = 0;
     for (int64_t i = lane; i < W; i += 32) s += __ldcg(p.team_kept + i);
 #pragma unroll
@@ -1492,8 +1495,10 @@ __global__ void __launch_bounds__(128) merge_kernel(const DecodeParams p, int64_
       else *p.stats = (uint32_t)s;
     }
   }
-  if (item >= (int64_t)U * P) return;
-  const int u = (int)(item / P), panel = (int)(item % P);
+  const int64_t item = blockIdx.x;
+  if (item >= (int64_t)U * P * GC) return;
+  const int g = (int)(item % GC);
+  const int u = (int)(item / (P * GC)), panel = (int)((item / GC) % P);
   const int* tp = p.tile_prefix;
   const int64_t N = tp[U];
   const int64_t WE = (N < W) ? (N > 0 ? N : 1) : W;
@@ -1503,63 +1508,68 @@ __global__ void __launch_bounds__(128) merge_kernel(const DecodeParams p, int64_
   if (w0 == w1) return;
   const int seq = u / (p.num_kv_heads * nchunks), kvh = (u / nchunks) % p.num_kv_heads, chunk = u % nchunks;
   const int gvalid = (p.group - chunk * GC) < GC ? (p.group - chunk * GC) : GC;
-  auto rec_of = [&](int64_t sl, int g) -> const float* { return p.part + ((sl * GC + g) * P + panel) * PST; };
+  if (g >= gvalid) return;
+  auto rec_of = [&](int64_t sl) -> const float* { return p.part + ((sl * GC + g) * P + panel) * PST; };
   const int n = (int)(w1 - w0 + 1);
   const int64_t sl0 = partial_slot(w0, R0, N, WE);
   auto slot_i = [&](int i) -> int64_t { return i == 0 ? sl0 : 2 * (w0 + i); };
   constexpr int NE = (HDL + 31) / 32;  // columns per lane
   constexpr int CH = NE <= 2 ? 16 : (NE <= 4 ? 8 : 4);  // partials whose accumulators are loaded together
-      for (int g = 0; g < gvalid; ++g) {
-        // (m, l) of partial `lane` and the accumulators of the first CH partials
-        // are loaded in the same round; M over all partials.
-        float mi = -INFINITY, li = 0.f;
-        if (lane < n) {
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec_of(slot_i(lane), g) + HDL));
-          mi = ml.x;
-          li = ml.y;
-        }
-        float a[NE];
+  const int per = (n + MW - 1) / MW;
+  const int i0 = wid * per, i1 = (i0 + per < n) ? i0 + per : n;
+  float Mw = -INFINITY, lw = 0.f, a[NE];
 #pragma unroll
-        for (int e = 0; e < NE; ++e) a[e] = 0.f;
-        float lt = 0.f, M = -INFINITY;
-        for (int b0 = 0; b0 < n; b0 += CH) {
-          float v[CH][NE];
+  for (int e = 0; e < NE; ++e) a[e] = 0.f;
+  if (i0 < i1) {
+    for (int i = i0 + lane; i < i1; i += 32) Mw = fmaxf(Mw, __ldcg(rec_of(slot_i(i)) + HDL));
+    Mw = warp_max(Mw);
+    for (int b0 = i0; b0 < i1; b0 += CH) {
+      float v[CH][NE];
 #pragma unroll
-          for (int k = 0; k < CH; ++k)
-#pragma unroll
-            for (int e = 0; e < NE; ++e)
-              v[k][e] = (b0 + k < n && lane + 32 * e < HDL) ? __ldcg(rec_of(slot_i(b0 + k), g) + lane + 32 * e) : 0.f;
-          if (b0 == 0) {
-            M = mi;
-            for (int i = lane + 32; i < n; i += 32) M = fmaxf(M, __ldcg(rec_of(slot_i(i), g) + HDL));
-            M = warp_max(M);
-          }
-          // weights of partials b0 .. b0+CH-1 (lanes hold partials 32 j + lane)
-          const int base32 = b0 & ~31;
-          float wt = 0.f;
-          if (base32 + lane < n) {
-            float mm = mi, ll = li;
-            if (base32 > 0) {
-              const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec_of(slot_i(base32 + lane), g) + HDL));
-              mm = ml.x;
-              ll = ml.y;
-            }
-            wt = exp2f(mm - M);
-            if (b0 == base32) lt = fmaf(ll, wt, lt);
-          }
-#pragma unroll
-          for (int k = 0; k < CH; ++k) {
-            const float w = __shfl_sync(0xffffffffu, wt, (b0 - base32 + k) & 31);
-#pragma unroll
-            for (int e = 0; e < NE; ++e) a[e] = fmaf(v[k][e], w, a[e]);
-          }
-        }
-        lt = warp_sum(lt);
+      for (int k = 0; k < CH; ++k)
 #pragma unroll
         for (int e = 0; e < NE; ++e)
-          if (lane + 32 * e < HDL)
-            emit(p, seq, kvh * p.group + chunk * GC + g, panel * HDL + lane + 32 * e, M, lt, a[e]);
+          v[k][e] = (b0 + k < i1 && lane + 32 * e < HDL) ? __ldcg(rec_of(slot_i(b0 + k)) + lane + 32 * e) : 0.f;
+      float wt = 0.f;  // lane k < CH: weight of partial b0 + k
+      if (lane < CH && b0 + lane < i1) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(rec_of(slot_i(b0 + lane)) + HDL));
+        wt = exp2f(ml.x - Mw);
+        lw = fmaf(ml.y, wt, lw);
       }
+#pragma unroll
+      for (int k = 0; k < CH; ++k) {
+        const float w = __shfl_sync(0xffffffffu, wt, k);
+#pragma unroll
+        for (int e = 0; e < NE; ++e) a[e] = fmaf(v[k][e], w, a[e]);
+      }
+    }
+    lw = warp_sum(lw);
+  }
+  __shared__ float s_m[MW], s_l[MW], s_a[MW][NE * 32];
+  if (lane == 0) {
+    s_m[wid] = Mw;
+    s_l[wid] = lw;
+  }
+#pragma unroll
+  for (int e = 0; e < NE; ++e) s_a[wid][lane + 32 * e] = a[e];
+  __syncthreads();
+  if (wid != 0) return;
+  float M = s_m[0];
+#pragma unroll
+  for (int w = 1; w < MW; ++w) M = fmaxf(M, s_m[w]);
+  float L = 0.f, o[NE];
+#pragma unroll
+  for (int e = 0; e < NE; ++e) o[e] = 0.f;
+#pragma unroll
+  for (int w = 0; w < MW; ++w) {
+    const float f = exp2f(s_m[w] - M);  // a warp without partials has m = -inf: weight 0
+    L = fmaf(s_l[w], f, L);
+#pragma unroll
+    for (int e = 0; e < NE; ++e) o[e] = fmaf(s_a[w][lane + 32 * e], f, o[e]);
+  }
+#pragma unroll
+  for (int e = 0; e < NE; ++e)
+    if (lane + 32 * e < HDL) emit(p, seq, kvh * p.group + chunk * GC + g, panel * HDL + lane + 32 * e, M, L, o[e]);
 }
 
 template <typename KT, typename VT, int HD, int GC, bool ATTN, int NSLOT, bool TC>
@@ -1605,10 +1615,9 @@ cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tk, const CU
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
   if (e != cudaSuccess || !ATTN) return e;
   // merge of the units shared by several teams: a programmatic dependent launch
-  constexpr int kMergeWarps = 4;
-  const int64_t items = (int64_t)p.num_seqs * p.num_kv_heads * nchunks * CF::P;
+  const int64_t items = (int64_t)p.num_seqs * p.num_kv_heads * nchunks * CF::P * GC;
   cudaLaunchConfig_t mc = {};
-  mc.gridDim = dim3((unsigned)((items + kMergeWarps - 1) / kMergeWarps));
+  mc.gridDim = dim3((unsigned)items);
   mc.blockDim = dim3(32 * kMergeWarps);
   mc.stream = stream;
   cudaLaunchAttribute ma[1];

@@ -86,6 +86,10 @@ class GatedLlama:
                             wo=w(s.heads * s.head_dim, s.hidden), ln2=ones(s.hidden),
                             w1=w(s.hidden, s.mlp), w3=w(s.hidden, s.mlp), w2=w(s.mlp, s.hidden))
                        for _ in range(s.layers)]
+        # one GEMV each for q|k|v and for the two MLP inputs (the same weights, concatenated)
+        for L in self.layers:
+            L["wqkv"] = torch.cat([L.pop("wq"), L.pop("wk"), L.pop("wv")], 1).contiguous()
+            L["w13"] = torch.cat([L.pop("w1"), L.pop("w3")], 1).contiguous()
         self.norm = ones(s.hidden)
         self.lm_head = w(s.hidden, s.vocab)
         # token-major caches (max_len, kv_heads, head_dim): a prefix [:n] is contiguous (what dense
@@ -108,15 +112,18 @@ class GatedLlama:
     def _qkv(self, L, h, pos):
         s = self.s
         T = h.shape[0]
-        q = (h @ L["wq"]).view(T, s.heads, s.head_dim).transpose(0, 1)
-        k = (h @ L["wk"]).view(T, s.kv_heads, s.head_dim).transpose(0, 1)
-        v = (h @ L["wv"]).view(T, s.kv_heads, s.head_dim).transpose(0, 1)
+        qkv = h @ L["wqkv"]
+        nq, nk = s.heads * s.head_dim, s.kv_heads * s.head_dim
+        q = qkv[:, :nq].view(T, s.heads, s.head_dim).transpose(0, 1)
+        k = qkv[:, nq:nq + nk].view(T, s.kv_heads, s.head_dim).transpose(0, 1)
+        v = qkv[:, nq + nk:].view(T, s.kv_heads, s.head_dim).transpose(0, 1)
         cos, sin = self._cos.index_select(0, pos), self._sin.index_select(0, pos)   # (T, hd) tables
         return _rope_t(q, cos, sin), _rope_t(k, cos, sin), v
 
     def _mlp(self, L, x):
         h = _rms(x, L["ln2"], self.s.eps)
-        return x + (F.silu(h @ L["w1"]) * (h @ L["w3"])) @ L["w2"]
+        a, b = (h @ L["w13"]).split(self.s.mlp, -1)
+        return x + (F.silu(a) * b) @ L["w2"]
 
     @torch.no_grad()
     def prefill(self, tokens: torch.Tensor) -> torch.Tensor:
@@ -208,14 +215,16 @@ class GatedLlama:
         idx = full_dev.long() + torch.arange(64, device=self.dev)
         valid = idx < npos
         idx = idx.clamp(max=self.max_len - 1)
-        kt = kc.index_select(1, idx).repeat_interleave(G, 0).float()      # (Hq, 64, hd)
-        vt = vc.index_select(1, idx).repeat_interleave(G, 0).float()
-        sc = (kt @ q.float()[:, :, None])[..., 0] * (LOG2E / math.sqrt(s.head_dim))
+        kt = kc.index_select(1, idx).float()                              # (KVH, 64, hd)
+        vt = vc.index_select(1, idx).float()
+        qg = q.float().view(s.kv_heads, G, s.head_dim)                    # a kv head's query group
+        sc = torch.bmm(qg, kt.transpose(1, 2)).view(s.heads, 64) * (LOG2E / math.sqrt(s.head_dim))
         sc = sc.masked_fill(~valid[None], float("-inf"))
         mt = sc.amax(-1).clamp(min=-1e9)                                 # an empty tail weighs 0
         pt = torch.exp2(sc - mt[:, None])
+        at = torch.bmm(pt.view(s.kv_heads, G, 64), vt).view(s.heads, s.head_dim)
         return merge_states(torch.stack([m, mt], 1).contiguous(), torch.stack([l, pt.sum(-1)], 1).contiguous(),
-                            torch.stack([acc, (pt[:, None, :] @ vt)[:, 0]], 1).contiguous(), self.dtype)
+                            torch.stack([acc, at], 1).contiguous(), self.dtype)
 
     @torch.no_grad()
     def _step_dev(self, tok, npos):
