@@ -266,6 +266,38 @@ int oc_fused_attention_tiles(const void* q, int q_dtype, int64_t q_seq_stride, i
                              float* acc_out, uint32_t* retained, uint32_t* status, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Decoder-step helpers of the model driver (orthocache_gpu_b200/model.py),
+ * the per-layer operations around the decode attention of a Llama-shaped
+ * model.  The reference runs them as PyTorch ops inside HF Llama (its
+ * evaluation harness, eval/perplexity_eval.py:320-745); here each is one
+ * launch so that a decode step is a short graph.  dtype: OC_BF16 or OC_F16.
+ *
+ * oc_add_rms_norm: per row of x (rows, n): x += y when y is not NULL (the
+ * residual add, rounded to dtype), then h = (x * rsqrt(mean(x^2) + eps))
+ * rounded to dtype, times weight (n), rounded to dtype. */
+int oc_add_rms_norm(void* x, const void* y, const void* weight, void* h, int64_t rows, int64_t n, float eps,
+                    int dtype, void* stream);
+
+/* oc_rope_cache_append: qkv (1, (heads + 2 kv_heads) head_dim) holds one
+ * token's q | k | v.  Writes the rotate-half rotary embedding of q (with the
+ * fp32 tables cos_tab / sin_tab (max_len, head_dim) at row *pos) to q_out
+ * (heads, head_dim), that of k to k_cache[*pos] and v to v_cache[*pos]; the
+ * caches are token-major (max_len, kv_heads, head_dim) with the given token
+ * stride.  *pos (int64) is read on the device. */
+int oc_rope_cache_append(const void* qkv, int heads, int kv_heads, int head_dim, const float* cos_tab,
+                         const float* sin_tab, const int64_t* pos, void* q_out, void* k_cache, void* v_cache,
+                         int64_t cache_token_stride, int dtype, void* stream);
+
+/* oc_tail_merge: decode attention of q (heads, head_dim) over the ragged
+ * tail of the caches, tokens [full, n) with n = *pos + 1 and full = n rounded
+ * down to 64, merged by log-sum-exp with the state (m in log2 units, l,
+ * unnormalised acc (heads, head_dim), float32) that the fused kernel returned
+ * for tokens [0, full) (oc_fused_attention_v3_shard).  scale_log2 =
+ * log2(e) / sqrt(head_dim).  out (heads, head_dim) in dtype. */
+int oc_tail_merge(const void* q, int heads, int kv_heads, int head_dim, const void* k_cache, const void* v_cache,
+                  int64_t cache_token_stride, int64_t max_len, const int64_t* pos, const float* m, const float* l,
+                  const float* acc, float scale_log2, void* out, int dtype, void* stream);
+
 /* Allocation-free variant of oc_fused_attention_v2 (no counterpart in the
  * reference).  For callers that cannot allocate device memory: code running
  * inside another framework's allocator, under a memory budget, or from a

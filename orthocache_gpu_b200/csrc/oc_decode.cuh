@@ -462,47 +462,58 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // LIST mode: the lists come from the gate kernel, launched just before as
   // this grid's programmatic predecessor; everything above overlapped it
   if (p.list_count != nullptr) asm volatile("griddepcontrol.wait;" ::: "memory");
-  // ---- tiles per unit, prefix in shared memory
-  for (int u = tid; u < U; u += blockDim.x) {
-    int T = p.num_tiles;
-    if (p.seq_lens != nullptr) {
-      const int L = p.seq_lens[u / (p.num_kv_heads * nchunks)];
-      if ((L < 0 || (L & 63) || L > p.num_tiles * 64) && blockIdx.x == 0) atomicOr(p.status, ST_BAD_SEQLEN);
-      const int lt = L < 0 ? 0 : (L >> 6);
-      T = lt < T ? lt : T;
-    }
-    if (p.list_count != nullptr) {
-      const int c = p.list_count[u / nchunks];
-      T = c < 0 ? 0 : (c < T ? c : T);
-    }
-    tp[u + 1] = T;
-  }
+  // ---- tiles per unit, prefix in shared memory.  Without per-sequence
+  // lengths or tile lists every unit has num_tiles tiles: each warp writes
+  // the whole prefix itself (every warp writes the same values), so no block
+  // barrier and no scan delay the first copies.
+  if (p.seq_lens == nullptr && p.list_count == nullptr) {
+    for (int u = lane; u <= U; u += 32) tp[u] = u * p.num_tiles;
+    __syncwarp();
 #ifdef OC_TRACE
-  __syncwarp();
-  tr_a = oc_clock();
+    tr_a = oc_clock();
 #endif
-  if (U <= 32 * 32) {  // one warp scans (up to 32 values a lane)
-    __syncthreads();
-    if (warp == 0) {
-      const int per = (U + 31) / 32, lo = 1 + lane * per, hi = min(U + 1, lo + per);
-      int run = 0;
-      for (int i = lo; i < hi; ++i) run += tp[i];
-      int inc = run;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += y;
-      }
-      int base = inc - run;
-      for (int i = lo; i < hi; ++i) {
-        base += tp[i];
-        tp[i] = base;
-      }
-      if (lane == 0) tp[0] = 0;
-    }
-    __syncthreads();
   } else {
-    block_scan(tp, U, scan_tmp);
+    for (int u = tid; u < U; u += blockDim.x) {
+      int T = p.num_tiles;
+      if (p.seq_lens != nullptr) {
+        const int L = p.seq_lens[u / (p.num_kv_heads * nchunks)];
+        if ((L < 0 || (L & 63) || L > p.num_tiles * 64) && blockIdx.x == 0) atomicOr(p.status, ST_BAD_SEQLEN);
+        const int lt = L < 0 ? 0 : (L >> 6);
+        T = lt < T ? lt : T;
+      }
+      if (p.list_count != nullptr) {
+        const int c = p.list_count[u / nchunks];
+        T = c < 0 ? 0 : (c < T ? c : T);
+      }
+      tp[u + 1] = T;
+    }
+#ifdef OC_TRACE
+    __syncwarp();
+    tr_a = oc_clock();
+#endif
+    if (U <= 32 * 32) {  // one warp scans (up to 32 values a lane)
+      __syncthreads();
+      if (warp == 0) {
+        const int per = (U + 31) / 32, lo = 1 + lane * per, hi = min(U + 1, lo + per);
+        int run = 0;
+        for (int i = lo; i < hi; ++i) run += tp[i];
+        int inc = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += y;
+        }
+        int base = inc - run;
+        for (int i = lo; i < hi; ++i) {
+          base += tp[i];
+          tp[i] = base;
+        }
+        if (lane == 0) tp[0] = 0;
+      }
+      __syncthreads();
+    } else {
+      block_scan(tp, U, scan_tmp);
+    }
   }
   const int64_t N = tp[U];
 #ifdef OC_TRACE
@@ -1467,7 +1478,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 // unit's partial states (log-sum-exp: running max M, weights 2^(m - M)), and
 // warp 0 combines the warps' states through shared memory and writes the
 // output.  Units held whole by one team were written directly.
-constexpr int kMergeWarps = 4;
+constexpr int kMergeWarps = 8;
 
 template <int HD, int GC, int P>
 __global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(const DecodeParams p, int64_t W) {

@@ -23,6 +23,7 @@ from typing import Dict, List, Optional
 import torch
 import torch.nn.functional as F
 
+from . import _lib
 from .distributed import merge_states, shard_partials
 
 LOG2E = 1.4426950408889634
@@ -201,47 +202,50 @@ class GatedLlama:
         return _rms(x, self.norm, s.eps) @ self.lm_head
 
     # ---------------------------------------------------------------- CUDA-graph decode
-    def _attend_dev(self, i, q, npos, full_dev):
-        """Decode attention with device-side lengths: npos (1,) int64 tokens in the cache,
-        full_dev (1,) int32 = npos rounded down to whole tiles.  Every shape is fixed,
-        so a step built from it can be captured once and replayed."""
-        s = self.s
-        G = s.heads // s.kv_heads
-        kc, vc = self.k_cache[i].transpose(0, 1), self.v_cache[i].transpose(0, 1)
-        cap = self.max_len - self.max_len % 64
-        m, l, acc, _ = shard_partials(q, kc[:, :cap], vc[:, :cap], self.tau[i], G, stats=False,
-                                      seq_len_dev=full_dev)
-        # the ragged tail: the 64 slots after the whole tiles, those at or beyond npos masked
-        idx = full_dev.long() + torch.arange(64, device=self.dev)
-        valid = idx < npos
-        idx = idx.clamp(max=self.max_len - 1)
-        kt = kc.index_select(1, idx).float()                              # (KVH, 64, hd)
-        vt = vc.index_select(1, idx).float()
-        qg = q.float().view(s.kv_heads, G, s.head_dim)                    # a kv head's query group
-        sc = torch.bmm(qg, kt.transpose(1, 2)).view(s.heads, 64) * (LOG2E / math.sqrt(s.head_dim))
-        sc = sc.masked_fill(~valid[None], float("-inf"))
-        mt = sc.amax(-1).clamp(min=-1e9)                                 # an empty tail weighs 0
-        pt = torch.exp2(sc - mt[:, None])
-        at = torch.bmm(pt.view(s.kv_heads, G, 64), vt).view(s.heads, s.head_dim)
-        return merge_states(torch.stack([m, mt], 1).contiguous(), torch.stack([l, pt.sum(-1)], 1).contiguous(),
-                            torch.stack([acc, at], 1).contiguous(), self.dtype)
-
     @torch.no_grad()
     def _step_dev(self, tok, npos):
         """One decode step from device state: tok (1,) next token, npos (1,) cache length;
-        both are updated in place (argmax token, length + 1)."""
+        both are updated in place (argmax token, length + 1).
+
+        The operations around the GEMVs and the fused decode attention are the
+        library's model-step kernels: residual add + RMSNorm, rotary embedding
+        + cache append at position npos, and the ragged-tail attention merged
+        with the kernel's softmax state (same arithmetic as ``step``)."""
         s = self.s
-        x = self.embed[tok]
-        n1 = npos + 1
-        full_dev = (torch.div(n1, 64, rounding_mode="floor") * 64).to(torch.int32)
+        lib, dev = _lib.load(), self.dev
+        st, dt = _lib.stream_ptr(dev), _lib.dtype_code(self.embed)
+        G = s.heads // s.kv_heads
+        x = self.embed[tok]                                           # (1, hidden) residual stream
+        h = torch.empty_like(x)
+        q = torch.empty((s.heads, s.head_dim), device=dev, dtype=self.dtype)
+        a = torch.empty_like(q)
+        full_dev = (torch.div(npos + 1, 64, rounding_mode="floor") * 64).to(torch.int32)
+        cap = self.max_len - self.max_len % 64
+        tok_stride = s.kv_heads * s.head_dim
+        y = None                                                      # the previous block's output
         for i, L in enumerate(self.layers):
-            q, k, v = self._qkv(L, _rms(x, L["ln1"], s.eps), npos)
-            self.k_cache[i].index_copy_(0, npos, k.transpose(0, 1))
-            self.v_cache[i].index_copy_(0, npos, v.transpose(0, 1))
-            a = self._attend_dev(i, q[:, 0].contiguous(), n1, full_dev)
-            x = x + a.reshape(1, -1) @ L["wo"]
-            x = self._mlp(L, x)
-        logits = _rms(x, self.norm, s.eps) @ self.lm_head
+            _lib.check(lib.oc_add_rms_norm(x.data_ptr(), _lib.ptr(y), L["ln1"].data_ptr(), h.data_ptr(), 1,
+                                           s.hidden, s.eps, dt, st), "oc_add_rms_norm")
+            qkv = h @ L["wqkv"]
+            _lib.check(lib.oc_rope_cache_append(qkv.data_ptr(), s.heads, s.kv_heads, s.head_dim,
+                                                self._cos.data_ptr(), self._sin.data_ptr(), npos.data_ptr(),
+                                                q.data_ptr(), self.k_cache[i].data_ptr(), self.v_cache[i].data_ptr(),
+                                                tok_stride, dt, st), "oc_rope_cache_append")
+            kc, vc = self.k_cache[i].transpose(0, 1), self.v_cache[i].transpose(0, 1)
+            m, l, acc, _ = shard_partials(q, kc[:, :cap], vc[:, :cap], self.tau[i], G, stats=False,
+                                          seq_len_dev=full_dev)
+            _lib.check(lib.oc_tail_merge(q.data_ptr(), s.heads, s.kv_heads, s.head_dim, self.k_cache[i].data_ptr(),
+                                         self.v_cache[i].data_ptr(), tok_stride, self.max_len, npos.data_ptr(),
+                                         m.data_ptr(), l.data_ptr(), acc.data_ptr(), LOG2E / math.sqrt(s.head_dim),
+                                         a.data_ptr(), dt, st), "oc_tail_merge")
+            o = a.view(1, -1) @ L["wo"]
+            _lib.check(lib.oc_add_rms_norm(x.data_ptr(), o.data_ptr(), L["ln2"].data_ptr(), h.data_ptr(), 1,
+                                           s.hidden, s.eps, dt, st), "oc_add_rms_norm")
+            g1, g3 = (h @ L["w13"]).split(s.mlp, -1)
+            y = (F.silu(g1) * g3) @ L["w2"]
+        _lib.check(lib.oc_add_rms_norm(x.data_ptr(), y.data_ptr(), self.norm.data_ptr(), h.data_ptr(), 1,
+                                       s.hidden, s.eps, dt, st), "oc_add_rms_norm")
+        logits = h @ self.lm_head
         tok.copy_(logits.argmax(-1))
         npos.add_(1)
         return logits
