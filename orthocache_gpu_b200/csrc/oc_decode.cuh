@@ -519,9 +519,14 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 #ifdef OC_TRACE
   tr_x[0] = oc_clock();
 #endif
-  if (ATTN && blockIdx.x == 0)
-    for (int u = tid; u <= U; u += blockDim.x) p.tile_prefix[u] = tp[u];
-
+  // Team wg owns the flattened K tiles [fa, fb) (see the single pass below)
+  const int64_t WE = (N < W) ? (N > 0 ? N : 1) : W;  // warps with a tile range
+#ifdef OC_TRACE
+  tr_x[1] = oc_clock();
+#endif
+  const bool active = wg < WE;
+  // flattened tile indices fit in 32 bits (at most 2048 units of 2^20 tiles): the loop uses int
+  const int fa = active ? (int)range_lo(wg, N, WE) : 0, fb = active ? (int)range_lo(wg + 1, N, WE) : 0;
   const uint64_t pol = policy_evict_first();
 
   auto unit_seq = [&](int u) { return u / (p.num_kv_heads * nchunks); };
@@ -652,6 +657,134 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
     return ring + s * SLOT;
   };
 
+  // ---- the first copies go out before the rest of the set-up
+  float2 qv[TC ? 1 : GC][D2];
+  uint32_t qf[TC ? HDL / 16 : 1][2];  // q (this warp's panel) as mma B fragments (dims x queries), raw 16-bit
+  int q_unit = -1;
+  uint32_t qf_pf[TC ? HDL / 16 : 1][2];  // prefetched fragments of unit pf_unit
+  int pf_unit = -1;
+  // q rows of a unit's query chunk (this warp's panel) as raw 16-bit mma B fragments
+  // The loads are issued unconditionally (lanes without a query read the
+  // chunk's first head) and nothing consumes them here, so the warp does not
+  // wait for them: qf_apply masks the lanes without a query when the
+  // fragments are first used.  q rows are 4-byte aligned (checked on the host).
+  auto load_qf = [&](int seq, int kvh, int chunk, uint32_t (&dst)[TC ? HDL / 16 : 1][2], bool& ok) {
+    if constexpr (TC) {
+      const int hq = chunk * GC + g8;
+      ok = g8 < GC && hq < p.group;
+      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+          static_cast<const uint16_t*>(p.q) + (int64_t)seq * p.q_seq_stride +
+          (int64_t)(kvh * p.group + (ok ? hq : chunk * GC)) * p.q_head_stride + panel * HDL);
+#pragma unroll
+      for (int ks = 0; ks < HDL / 16; ++ks) {
+        dst[ks][0] = qrow[8 * ks + t4];
+        dst[ks][1] = qrow[8 * ks + t4 + 4];
+      }
+    }
+  };
+  bool qok_pf = false;
+  auto qf_apply = [&](const uint32_t (&src)[TC ? HDL / 16 : 1][2], bool ok) {
+#pragma unroll
+    for (int ks = 0; ks < (TC ? HDL / 16 : 1); ++ks) {
+      qf[ks][0] = ok ? src[ks][0] : 0u;
+      qf[ks][1] = ok ? src[ks][1] : 0u;
+    }
+  };
+
+  // descriptor of ring slot `lane` (lanes < NSLOT): flattened tile (-1: empty),
+  // V copy flag, unit and tile index
+  //   dsc_a = 2 * (f - fa) + (V copy), or -1 for an empty slot; dsc_b = (unit << 20) | tile
+  int dsc_a = -1, dsc_b = 0;
+#ifdef OC_TRACE
+  tr_x[3] = oc_clock();
+#endif
+  const int u_first = (fb > fa) ? upper_index(tp, U, fa) : 0;
+  int u_iss = u_first, seq_iss = 0, kvh_iss = 0;
+  int u_end_iss = 0;  // first flattened tile after unit u_iss
+  int f_iss = fa;
+  SplitIter it_iss;
+  // GATE_LIST: list entry of the next tile to issue, loaded one issue ahead
+  int list_pf = 0;
+  auto list_load = [&](int u, int f) {
+    return p.tile_list[(int64_t)(u / nchunks) * p.list_stride + (f - tp[u])];
+  };
+  auto enter_unit = [&](int u, int f) {  // issue cursor enters unit u at flattened tile f
+    u_iss = u;
+    u_end_iss = tp[u + 1];
+    seq_iss = unit_seq(u);
+    kvh_iss = unit_kvh(u);
+    if constexpr (ATTN && TC) {
+      load_qf(seq_iss, kvh_iss, unit_chunk(u), qf_pf, qok_pf);
+      pf_unit = u;
+    }
+    it_iss.init((int)(f - tp[u]), tp[u + 1] - tp[u], S);
+    if (p.tile_list != nullptr) list_pf = list_load(u, f);
+  };
+#ifdef OC_TRACE
+  tr_b = oc_clock();
+#endif
+  if (fb > fa) enter_unit(u_first, fa);
+#ifdef OC_TRACE
+  unsigned long long tr_c = oc_clock(), tr_d = 0;
+#endif
+  // LIST mode: every tile is retained, so a tile's V copy is issued into the
+  // slot right after its K copy (both in flight at once); the V item reads
+  // the logits its K item left in the preceding slot's logit area.
+#ifndef OC_LIST_PAIRED
+#define OC_LIST_PAIRED 0  // measured slower (192 vs 209 us at the V3 shapes); kept as a build option
+#endif
+  const bool paired = OC_LIST_PAIRED && ATTN && p.tile_list != nullptr;
+  int pend_v = 0, pv_seq = 0, pv_kvh = 0, pv_tile = 0, pv_da = 0, pv_u = 0;
+  auto issue_next = [&](uint32_t s) {
+    if (paired && pend_v) {
+      issue(s, pv_seq, pv_kvh, pv_tile, true);
+      if (lane == (int)s) {
+        dsc_a = pv_da | 1;
+        dsc_b = (pv_u << 20) | pv_tile;
+      }
+      pend_v = 0;
+      return;
+    }
+    if (f_iss < fb) {
+      if (f_iss >= u_end_iss) {
+        int u = u_iss + 1;
+        while (f_iss >= tp[u + 1]) ++u;
+        enter_unit(u, f_iss);
+      }
+      const int tile = p.tile_list != nullptr ? list_pf : it_iss.tile();
+      issue(s, seq_iss, kvh_iss, tile, false);
+      if (lane == (int)s) {
+        dsc_a = 2 * (int)(f_iss - fa);
+        dsc_b = (u_iss << 20) | tile;
+      }
+      if (paired) {
+        pend_v = 1;
+        pv_seq = seq_iss;
+        pv_kvh = kvh_iss;
+        pv_tile = tile;
+        pv_da = 2 * (int)(f_iss - fa);
+        pv_u = u_iss;
+      }
+      it_iss.next();
+      ++f_iss;
+      if (p.tile_list != nullptr && f_iss < u_end_iss && f_iss < fb) list_pf = list_load(u_iss, f_iss);
+    } else if (lane == (int)s) {
+      dsc_a = -1;
+    }
+  };
+  for (uint32_t s = 0; s < NSLOT; ++s) {
+    issue_next(s);
+#ifdef OC_TRACE
+    if (s == 0) tr_d = oc_clock();
+#endif
+  }
+#ifdef OC_TRACE
+  tr_t1 = oc_clock();
+#endif
+
+  if (ATTN && blockIdx.x == 0)
+    for (int u = tid; u <= U; u += blockDim.x) p.tile_prefix[u] = tp[u];
+
   float qmax = 0.f;  // max_g |q_g| of the current unit (Cauchy-Schwarz gate)
   uint32_t ktiles = 0;  // K tiles gated (selects the team's exchange buffer)
   // ---- tensor-core gate constants.  The gate runs with the K tile as the A
@@ -744,13 +877,6 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   // the ring is one FIFO of copies.  A unit's state is written once all its K
   // tiles in the range are gated and no V copy of it is pending: directly when
   // the range holds the whole unit, else as a partial state for merge_kernel.
-  const int64_t WE = (N < W) ? (N > 0 ? N : 1) : W;  // warps with a tile range
-#ifdef OC_TRACE
-  tr_x[1] = oc_clock();
-#endif
-  const bool active = wg < WE;
-  // flattened tile indices fit in 32 bits (at most 2048 units of 2^20 tiles): the loop uses int
-  const int fa = active ? (int)range_lo(wg, N, WE) : 0, fb = active ? (int)range_lo(wg + 1, N, WE) : 0;
   int kept_stat = 0;
   if constexpr (ATTN) {
     // units without a tile: zero output (or an empty partial state)
@@ -886,129 +1012,6 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 
   reset_state();
 
-  float2 qv[TC ? 1 : GC][D2];
-  uint32_t qf[TC ? HDL / 16 : 1][2];  // q (this warp's panel) as mma B fragments (dims x queries), raw 16-bit
-  int q_unit = -1;
-  uint32_t qf_pf[TC ? HDL / 16 : 1][2];  // prefetched fragments of unit pf_unit
-  int pf_unit = -1;
-  // q rows of a unit's query chunk (this warp's panel) as raw 16-bit mma B fragments
-  // The loads are issued unconditionally (lanes without a query read the
-  // chunk's first head) and nothing consumes them here, so the warp does not
-  // wait for them: qf_apply masks the lanes without a query when the
-  // fragments are first used.  q rows are 4-byte aligned (checked on the host).
-  auto load_qf = [&](int seq, int kvh, int chunk, uint32_t (&dst)[TC ? HDL / 16 : 1][2], bool& ok) {
-    if constexpr (TC) {
-      const int hq = chunk * GC + g8;
-      ok = g8 < GC && hq < p.group;
-      const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-          static_cast<const uint16_t*>(p.q) + (int64_t)seq * p.q_seq_stride +
-          (int64_t)(kvh * p.group + (ok ? hq : chunk * GC)) * p.q_head_stride + panel * HDL);
-#pragma unroll
-      for (int ks = 0; ks < HDL / 16; ++ks) {
-        dst[ks][0] = qrow[8 * ks + t4];
-        dst[ks][1] = qrow[8 * ks + t4 + 4];
-      }
-    }
-  };
-  bool qok_pf = false;
-  auto qf_apply = [&](const uint32_t (&src)[TC ? HDL / 16 : 1][2], bool ok) {
-#pragma unroll
-    for (int ks = 0; ks < (TC ? HDL / 16 : 1); ++ks) {
-      qf[ks][0] = ok ? src[ks][0] : 0u;
-      qf[ks][1] = ok ? src[ks][1] : 0u;
-    }
-  };
-
-  // descriptor of ring slot `lane` (lanes < NSLOT): flattened tile (-1: empty),
-  // V copy flag, unit and tile index
-  //   dsc_a = 2 * (f - fa) + (V copy), or -1 for an empty slot; dsc_b = (unit << 20) | tile
-  int dsc_a = -1, dsc_b = 0;
-#ifdef OC_TRACE
-  tr_x[3] = oc_clock();
-#endif
-  const int u_first = (fb > fa) ? upper_index(tp, U, fa) : 0;
-  int u_iss = u_first, seq_iss = 0, kvh_iss = 0;
-  int u_end_iss = 0;  // first flattened tile after unit u_iss
-  int f_iss = fa;
-  SplitIter it_iss;
-  // GATE_LIST: list entry of the next tile to issue, loaded one issue ahead
-  int list_pf = 0;
-  auto list_load = [&](int u, int f) {
-    return p.tile_list[(int64_t)(u / nchunks) * p.list_stride + (f - tp[u])];
-  };
-  auto enter_unit = [&](int u, int f) {  // issue cursor enters unit u at flattened tile f
-    u_iss = u;
-    u_end_iss = tp[u + 1];
-    seq_iss = unit_seq(u);
-    kvh_iss = unit_kvh(u);
-    if constexpr (ATTN && TC) {
-      load_qf(seq_iss, kvh_iss, unit_chunk(u), qf_pf, qok_pf);
-      pf_unit = u;
-    }
-    it_iss.init((int)(f - tp[u]), tp[u + 1] - tp[u], S);
-    if (p.tile_list != nullptr) list_pf = list_load(u, f);
-  };
-#ifdef OC_TRACE
-  tr_b = oc_clock();
-#endif
-  if (fb > fa) enter_unit(u_first, fa);
-#ifdef OC_TRACE
-  unsigned long long tr_c = oc_clock(), tr_d = 0;
-#endif
-  // LIST mode: every tile is retained, so a tile's V copy is issued into the
-  // slot right after its K copy (both in flight at once); the V item reads
-  // the logits its K item left in the preceding slot's logit area.
-#ifndef OC_LIST_PAIRED
-#define OC_LIST_PAIRED 0  // measured slower (192 vs 209 us at the V3 shapes); kept as a build option
-#endif
-  const bool paired = OC_LIST_PAIRED && ATTN && p.tile_list != nullptr;
-  int pend_v = 0, pv_seq = 0, pv_kvh = 0, pv_tile = 0, pv_da = 0, pv_u = 0;
-  auto issue_next = [&](uint32_t s) {
-    if (paired && pend_v) {
-      issue(s, pv_seq, pv_kvh, pv_tile, true);
-      if (lane == (int)s) {
-        dsc_a = pv_da | 1;
-        dsc_b = (pv_u << 20) | pv_tile;
-      }
-      pend_v = 0;
-      return;
-    }
-    if (f_iss < fb) {
-      if (f_iss >= u_end_iss) {
-        int u = u_iss + 1;
-        while (f_iss >= tp[u + 1]) ++u;
-        enter_unit(u, f_iss);
-      }
-      const int tile = p.tile_list != nullptr ? list_pf : it_iss.tile();
-      issue(s, seq_iss, kvh_iss, tile, false);
-      if (lane == (int)s) {
-        dsc_a = 2 * (int)(f_iss - fa);
-        dsc_b = (u_iss << 20) | tile;
-      }
-      if (paired) {
-        pend_v = 1;
-        pv_seq = seq_iss;
-        pv_kvh = kvh_iss;
-        pv_tile = tile;
-        pv_da = 2 * (int)(f_iss - fa);
-        pv_u = u_iss;
-      }
-      it_iss.next();
-      ++f_iss;
-      if (p.tile_list != nullptr && f_iss < u_end_iss && f_iss < fb) list_pf = list_load(u_iss, f_iss);
-    } else if (lane == (int)s) {
-      dsc_a = -1;
-    }
-  };
-  for (uint32_t s = 0; s < NSLOT; ++s) {
-    issue_next(s);
-#ifdef OC_TRACE
-    if (s == 0) tr_d = oc_clock();
-#endif
-  }
-#ifdef OC_TRACE
-  tr_t1 = oc_clock();
-#endif
 
   int u_k = -1, kept_k = 0;  // unit of the last gated K tile and its retained tiles in the range
   int seq_k = 0, kvh_k = 0, chunk_k = 0;
