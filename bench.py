@@ -455,10 +455,13 @@ def extra_configs(dev, rank, world, dist, peak):
         m = GatedLlama(LlamaShape(), max_len=16384 + 320, device=dev, seed=5)
         prompt = torch.randint(0, 32000, (16384,), generator=g, device=dev)
         row = {"config": "TinyLlama-1.1B-shaped random-init, 22 layers, 32Q/4KV, hd 64, bf16, 16K prompt, "
-                         "256 greedy steps: the decode step replayed from one CUDA graph, and eager steps (median)",
+                         "256 greedy steps: the decode step replayed from one CUDA graph (fused kernel; dense arm: the same "
+                         "step with flashinfer decode over the 16K prompt), and eager steps (median)",
                "weight_read_bound_ms": round(m.weight_bytes() / (peak * 1e9) * 1e3, 3)}
         r = m.generate_graph(prompt, 256, tau_mode="median")
         row["fused_graph_ms_per_token"] = round(r["ms_per_token"], 3)
+        r = m.generate_graph(prompt, 256, dense=True)
+        row["dense_flashinfer_graph_ms_per_token"] = round(r["ms_per_token"], 3)
         for mode, key in (("median", "fused_eager_ms_per_token"), ("flash", "dense_flashinfer_eager_ms_per_token")):
             r = m.generate(prompt, 256, tau_mode=mode)
             row[key] = round(r["ms_per_token"], 3)

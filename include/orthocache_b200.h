@@ -298,6 +298,33 @@ int oc_tail_merge(const void* q, int heads, int kv_heads, int head_dim, const vo
                   int64_t cache_token_stride, int64_t max_len, const int64_t* pos, const float* m, const float* l,
                   const float* acc, float scale_log2, void* out, int dtype, void* stream);
 
+/* oc_gemv: one decode token's projection out[n] = sum_k h[k] W[n, k], W in
+ * the (out_features, in_features) layout of a linear layer (N rows of K
+ * contiguous 16-bit elements, leading dimension ldw; K and ldw multiples of
+ * 8, K <= 8192, N even, W 16-byte aligned), fp32 accumulation.  With
+ * norm_w == NULL, h = x.  With norm_w, the residual add and RMSNorm of
+ * oc_add_rms_norm run first, inside the same launch: v = round(x + y) (y may
+ * be NULL), written to x_out when x_out is not NULL (it must not alias x or
+ * y), and h = rmsnorm(v, eps) * norm_w (x / y / x_out 16-byte aligned).
+ * epilogue OC_GEMV_PLAIN: out (N) = round(h W^T).  OC_GEMV_SILU_MUL: W's
+ * rows interleave two projections, row 2j = a_j and row 2j + 1 = b_j, and
+ * out (N / 2) = round(round(silu(round(a))) * round(b)).  The launch is a
+ * programmatic dependent of the kernel before it on the stream.  The
+ * reference runs these products as PyTorch linear layers inside HF Llama
+ * (eval/perplexity_eval.py:320-745). */
+enum { OC_GEMV_PLAIN = 0, OC_GEMV_SILU_MUL = 1 };
+int oc_gemv(const void* x, const void* y, const void* norm_w, float eps, void* x_out, const void* W, int64_t ldw,
+            int64_t K, int64_t N, void* out, int epilogue, int dtype, void* stream);
+
+/* oc_gemv_qkv_rope: oc_gemv with N = (heads + 2 kv_heads) head_dim rows
+ * (q | k | v) whose epilogue is oc_rope_cache_append's: the rotary embedding
+ * of the q and k rows at position *pos, q to q_out (heads, head_dim), k and v
+ * written to the token-major caches at *pos (head_dim even). */
+int oc_gemv_qkv_rope(const void* x, const void* y, const void* norm_w, float eps, void* x_out, const void* W,
+                     int64_t ldw, int64_t K, int heads, int kv_heads, int head_dim, const float* cos_tab,
+                     const float* sin_tab, const int64_t* pos, void* q_out, void* k_cache, void* v_cache,
+                     int64_t cache_token_stride, int dtype, void* stream);
+
 /* Allocation-free variant of oc_fused_attention_v2 (no counterpart in the
  * reference).  For callers that cannot allocate device memory: code running
  * inside another framework's allocator, under a memory budget, or from a

@@ -59,6 +59,9 @@ SIGNATURES = {
     "oc_lse_merge": (_i, [_vp, _vp, _vp, _i64, _i, _i, _vp, _i, _vp]),
     "oc_add_rms_norm": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, C.c_float, _i, _vp]),
     "oc_rope_cache_append": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i, _vp]),
+    "oc_gemv": (_i, [_vp, _vp, _vp, C.c_float, _vp, _vp, _i64, _i64, _i64, _vp, _i, _i, _vp]),
+    "oc_gemv_qkv_rope": (_i, [_vp, _vp, _vp, C.c_float, _vp, _vp, _i64, _i64, _i, _i, _i, _vp, _vp, _vp, _vp, _vp,
+                              _vp, _i64, _i, _vp]),
     "oc_tail_merge": (_i, [_vp, _i, _i, _i, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, C.c_float, _vp, _i, _vp]),
     "oc_fused_attention_v3_shard": (_i, [_vp, _i, _i64, _vp, _i, _i64, _i64, _vp, _i, _i64, _i64, _i, _i, _i64,
                                          _i, _d, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),

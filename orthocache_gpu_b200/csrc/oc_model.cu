@@ -121,14 +121,26 @@ __global__ void tail_merge_kernel(const T* q, int group, int hd, const T* k_cach
                                   const float* l_in, const float* acc_in, float scale_log2, T* out) {
   __shared__ float red[32];
   __shared__ float pt[64];
+  __shared__ float qs[256];
   const int h = blockIdx.x, kvh = h / group, t = threadIdx.x;
   const int64_t n = *pos_p + 1, full = n - (n & 63);
-  const int64_t tok = full + t;
-  const int64_t row = (tok < max_len ? tok : max_len - 1) * tok_stride + (int64_t)kvh * hd;
+  const int r = (int)(n - full);  // tail tokens
+  for (int d = t; d < hd; d += blockDim.x) qs[d] = ld(q, (int64_t)h * hd + d);
+  __syncthreads();
   float lg = -INFINITY;
-  if (tok < n) {
+  if (t < r) {
+    const T* kr = k_cache + (full + t) * tok_stride + (int64_t)kvh * hd;
     float s = 0.f;
-    for (int d = 0; d < hd; ++d) s = fmaf(ld(q, (int64_t)h * hd + d), ld(k_cache, row + d), s);
+    if ((hd & 7) == 0 && ((reinterpret_cast<uintptr_t>(kr) & 15u) == 0)) {
+      for (int d = 0; d < hd; d += 8) {  // 16-byte loads of the key row
+        const uint4 u = *reinterpret_cast<const uint4*>(kr + d);
+        const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s = fmaf(qs[d + j], ld(e, j), s);
+      }
+    } else {
+      for (int d = 0; d < hd; ++d) s = fmaf(qs[d], ld(kr, d), s);
+    }
     lg = s * scale_log2;
   }
   const float mt = fmaxf(block_max(lg, red), -1e9f);  // an empty tail weighs 0
@@ -139,11 +151,10 @@ __global__ void tail_merge_kernel(const T* q, int group, int hd, const T* k_cach
   const float a = exp2f(m0 - M), b = exp2f(mt - M);
   const float L = fmaf(l_in[h], a, lt * b);
   for (int d = t; d < hd; d += blockDim.x) {
+    const T* vc = v_cache + full * tok_stride + (int64_t)kvh * hd + d;
     float s = 0.f;
-    for (int j = 0; j < 64; ++j) {
-      const int64_t tj = full + j;
-      if (tj < n) s = fmaf(pt[j], ld(v_cache, tj * tok_stride + (int64_t)kvh * hd + d), s);
-    }
+#pragma unroll 8
+    for (int j = 0; j < r; ++j) s = fmaf(pt[j], ld(vc, (int64_t)j * tok_stride), s);
     out[(int64_t)h * hd + d] = rnd<T>(fmaf(acc_in[(int64_t)h * hd + d], a, s * b) / fmaxf(L, 1e-9f));
   }
 }
@@ -199,7 +210,7 @@ extern "C" int oc_tail_merge(const void* q, int heads, int kv_heads, int head_di
                              const float* m, const float* l, const float* acc, float scale_log2, void* out,
                              int dtype, void* stream) {
   if (!q || !k_cache || !v_cache || !pos || !m || !l || !acc || !out || heads < 1 || kv_heads < 1 ||
-      heads % kv_heads || head_dim < 1 || max_len < 1)
+      heads % kv_heads || head_dim < 1 || head_dim > 256 || max_len < 1)
     return OC_ERR_INVALID;
   auto st = static_cast<cudaStream_t>(stream);
   const int group = heads / kv_heads;

@@ -87,12 +87,18 @@ class GatedLlama:
                             wo=w(s.heads * s.head_dim, s.hidden), ln2=ones(s.hidden),
                             w1=w(s.hidden, s.mlp), w3=w(s.hidden, s.mlp), w2=w(s.mlp, s.hidden))
                        for _ in range(s.layers)]
-        # one GEMV each for q|k|v and for the two MLP inputs (the same weights, concatenated)
+        # weights in the (out_features, in_features) layout of a linear layer (each output a
+        # contiguous row); one GEMV each for q|k|v and for the two MLP inputs (the same weights,
+        # concatenated; w1 | w3 rows interleaved, row 2j = w1's output j and row 2j + 1 = w3's,
+        # the layout of oc_gemv's SILU_MUL epilogue)
         for L in self.layers:
-            L["wqkv"] = torch.cat([L.pop("wq"), L.pop("wk"), L.pop("wv")], 1).contiguous()
-            L["w13"] = torch.cat([L.pop("w1"), L.pop("w3")], 1).contiguous()
+            L["wqkv"] = torch.cat([L.pop("wq"), L.pop("wk"), L.pop("wv")], 1).t().contiguous()
+            w1, w3 = L.pop("w1"), L.pop("w3")
+            L["w13"] = torch.stack([w1.t(), w3.t()], 1).reshape(2 * s.mlp, s.hidden).contiguous()
+            L["wo"] = L["wo"].t().contiguous()
+            L["w2"] = L["w2"].t().contiguous()
         self.norm = ones(s.hidden)
-        self.lm_head = w(s.hidden, s.vocab)
+        self.lm_head = w(s.hidden, s.vocab).t().contiguous()
         # token-major caches (max_len, kv_heads, head_dim): a prefix [:n] is contiguous (what dense
         # flash-decoding wants); the fused kernel reads the (kv_heads, n, head_dim) view through its strides
         self.k_cache = [torch.zeros(max_len, s.kv_heads, s.head_dim, device=self.dev, dtype=dtype)
@@ -113,7 +119,7 @@ class GatedLlama:
     def _qkv(self, L, h, pos):
         s = self.s
         T = h.shape[0]
-        qkv = h @ L["wqkv"]
+        qkv = F.linear(h, L["wqkv"])
         nq, nk = s.heads * s.head_dim, s.kv_heads * s.head_dim
         q = qkv[:, :nq].view(T, s.heads, s.head_dim).transpose(0, 1)
         k = qkv[:, nq:nq + nk].view(T, s.kv_heads, s.head_dim).transpose(0, 1)
@@ -123,8 +129,8 @@ class GatedLlama:
 
     def _mlp(self, L, x):
         h = _rms(x, L["ln2"], self.s.eps)
-        a, b = (h @ L["w13"]).split(self.s.mlp, -1)
-        return x + (F.silu(a) * b) @ L["w2"]
+        ab = F.linear(h, L["w13"]).view(*h.shape[:-1], -1, 2)
+        return x + F.linear(F.silu(ab[..., 0]) * ab[..., 1], L["w2"])
 
     @torch.no_grad()
     def prefill(self, tokens: torch.Tensor) -> torch.Tensor:
@@ -138,10 +144,10 @@ class GatedLlama:
             self.k_cache[i][:T] = k.transpose(0, 1)
             self.v_cache[i][:T] = v.transpose(0, 1)
             a = F.scaled_dot_product_attention(q[None], k[None], v[None], is_causal=True, enable_gqa=True)[0]
-            x = x + a.transpose(0, 1).reshape(T, -1) @ L["wo"]
+            x = x + F.linear(a.transpose(0, 1).reshape(T, -1), L["wo"])
             x = self._mlp(L, x)
         self.length = T
-        return _rms(x[-1:], self.norm, s.eps) @ self.lm_head
+        return F.linear(_rms(x[-1:], self.norm, s.eps), self.lm_head)
 
     # ---------------------------------------------------------------- decode
     def _median_bound(self, q, k_tiles):
@@ -196,74 +202,96 @@ class GatedLlama:
             self.length += 1
             a = self._attend(i, q[:, 0].contiguous(), tau_mode)
             self.length -= 1
-            x = x + a.reshape(1, -1) @ L["wo"]
+            x = x + F.linear(a.reshape(1, -1), L["wo"])
             x = self._mlp(L, x)
         self.length += 1
-        return _rms(x, self.norm, s.eps) @ self.lm_head
+        return F.linear(_rms(x, self.norm, s.eps), self.lm_head)
 
     # ---------------------------------------------------------------- CUDA-graph decode
     @torch.no_grad()
-    def _step_dev(self, tok, npos):
+    def _step_dev(self, tok, npos, dense_window: Optional[int] = None):
         """One decode step from device state: tok (1,) next token, npos (1,) cache length;
         both are updated in place (argmax token, length + 1).
 
-        The operations around the GEMVs and the fused decode attention are the
-        library's model-step kernels: residual add + RMSNorm, rotary embedding
-        + cache append at position npos, and the ragged-tail attention merged
-        with the kernel's softmax state (same arithmetic as ``step``)."""
+        Eight launches per layer: the q|k|v GEMV with the residual add + RMSNorm
+        in its prologue and rotary embedding + cache append in its epilogue;
+        the fused decode attention over whole tiles (+ its merge) and the
+        ragged-tail merge; the output projection; the MLP input GEMV (residual
+        add + RMSNorm prologue, silu(a) * b epilogue); the MLP output
+        projection.  Same arithmetic as ``step`` up to fp32 summation order.
+        ``dense_window``: timing arm only -- dense flash-decoding (flashinfer)
+        of the first ``dense_window`` cached tokens instead of the fused
+        kernel (a CUDA graph needs a fixed length for it)."""
         s = self.s
         lib, dev = _lib.load(), self.dev
         st, dt = _lib.stream_ptr(dev), _lib.dtype_code(self.embed)
         G = s.heads // s.kv_heads
-        x = self.embed[tok]                                           # (1, hidden) residual stream
-        h = torch.empty_like(x)
+        res = [self.embed[tok].contiguous(), torch.empty((1, s.hidden), device=dev, dtype=self.dtype)]
         q = torch.empty((s.heads, s.head_dim), device=dev, dtype=self.dtype)
         a = torch.empty_like(q)
+        o = torch.empty((1, s.hidden), device=dev, dtype=self.dtype)
+        g = torch.empty((1, s.mlp), device=dev, dtype=self.dtype)
+        y = torch.empty((1, s.hidden), device=dev, dtype=self.dtype)
         full_dev = (torch.div(npos + 1, 64, rounding_mode="floor") * 64).to(torch.int32)
         cap = self.max_len - self.max_len % 64
         tok_stride = s.kv_heads * s.head_dim
-        y = None                                                      # the previous block's output
+        cur, prev_y = 0, None
         for i, L in enumerate(self.layers):
-            _lib.check(lib.oc_add_rms_norm(x.data_ptr(), _lib.ptr(y), L["ln1"].data_ptr(), h.data_ptr(), 1,
-                                           s.hidden, s.eps, dt, st), "oc_add_rms_norm")
-            qkv = h @ L["wqkv"]
-            _lib.check(lib.oc_rope_cache_append(qkv.data_ptr(), s.heads, s.kv_heads, s.head_dim,
-                                                self._cos.data_ptr(), self._sin.data_ptr(), npos.data_ptr(),
-                                                q.data_ptr(), self.k_cache[i].data_ptr(), self.v_cache[i].data_ptr(),
-                                                tok_stride, dt, st), "oc_rope_cache_append")
-            kc, vc = self.k_cache[i].transpose(0, 1), self.v_cache[i].transpose(0, 1)
-            m, l, acc, _ = shard_partials(q, kc[:, :cap], vc[:, :cap], self.tau[i], G, stats=False,
-                                          seq_len_dev=full_dev)
-            _lib.check(lib.oc_tail_merge(q.data_ptr(), s.heads, s.kv_heads, s.head_dim, self.k_cache[i].data_ptr(),
-                                         self.v_cache[i].data_ptr(), tok_stride, self.max_len, npos.data_ptr(),
-                                         m.data_ptr(), l.data_ptr(), acc.data_ptr(), LOG2E / math.sqrt(s.head_dim),
-                                         a.data_ptr(), dt, st), "oc_tail_merge")
-            o = a.view(1, -1) @ L["wo"]
-            _lib.check(lib.oc_add_rms_norm(x.data_ptr(), o.data_ptr(), L["ln2"].data_ptr(), h.data_ptr(), 1,
-                                           s.hidden, s.eps, dt, st), "oc_add_rms_norm")
-            g1, g3 = (h @ L["w13"]).split(s.mlp, -1)
-            y = (F.silu(g1) * g3) @ L["w2"]
-        _lib.check(lib.oc_add_rms_norm(x.data_ptr(), y.data_ptr(), self.norm.data_ptr(), h.data_ptr(), 1,
-                                       s.hidden, s.eps, dt, st), "oc_add_rms_norm")
-        logits = h @ self.lm_head
+            _lib.check(lib.oc_gemv_qkv_rope(
+                res[cur].data_ptr(), _lib.ptr(prev_y), L["ln1"].data_ptr(), s.eps, res[1 - cur].data_ptr(),
+                L["wqkv"].data_ptr(), L["wqkv"].stride(0), s.hidden, s.heads, s.kv_heads, s.head_dim,
+                self._cos.data_ptr(), self._sin.data_ptr(), npos.data_ptr(), q.data_ptr(),
+                self.k_cache[i].data_ptr(), self.v_cache[i].data_ptr(), tok_stride, dt, st),
+                "oc_gemv_qkv_rope")
+            cur = 1 - cur
+            if dense_window is not None:
+                import flashinfer
+                a = flashinfer.single_decode_with_kv_cache(q, self.k_cache[i][:dense_window],
+                                                           self.v_cache[i][:dense_window], kv_layout="NHD")
+            else:
+                kc, vc = self.k_cache[i].transpose(0, 1), self.v_cache[i].transpose(0, 1)
+                m, l, acc, _ = shard_partials(q, kc[:, :cap], vc[:, :cap], self.tau[i], G, stats=False,
+                                              seq_len_dev=full_dev)
+                _lib.check(lib.oc_tail_merge(q.data_ptr(), s.heads, s.kv_heads, s.head_dim,
+                                             self.k_cache[i].data_ptr(), self.v_cache[i].data_ptr(), tok_stride,
+                                             self.max_len, npos.data_ptr(), m.data_ptr(), l.data_ptr(),
+                                             acc.data_ptr(), LOG2E / math.sqrt(s.head_dim), a.data_ptr(), dt, st),
+                           "oc_tail_merge")
+            _lib.check(lib.oc_gemv(a.data_ptr(), 0, 0, 0.0, 0, L["wo"].data_ptr(), L["wo"].stride(0),
+                                   s.heads * s.head_dim, s.hidden, o.data_ptr(), 0, dt, st), "oc_gemv")
+            _lib.check(lib.oc_gemv(res[cur].data_ptr(), o.data_ptr(), L["ln2"].data_ptr(), s.eps,
+                                   res[1 - cur].data_ptr(), L["w13"].data_ptr(), L["w13"].stride(0), s.hidden,
+                                   2 * s.mlp, g.data_ptr(), 1, dt, st), "oc_gemv")
+            cur = 1 - cur
+            _lib.check(lib.oc_gemv(g.data_ptr(), 0, 0, 0.0, 0, L["w2"].data_ptr(), L["w2"].stride(0), s.mlp,
+                                   s.hidden, y.data_ptr(), 0, dt, st), "oc_gemv")
+            prev_y = y
+        logits = torch.empty((1, s.vocab), device=dev, dtype=self.dtype)
+        _lib.check(lib.oc_gemv(res[cur].data_ptr(), y.data_ptr(), self.norm.data_ptr(), s.eps, 0,
+                               self.lm_head.data_ptr(), self.lm_head.stride(0), s.hidden, s.vocab,
+                               logits.data_ptr(), 0, dt, st), "oc_gemv")
         tok.copy_(logits.argmax(-1))
         npos.add_(1)
         return logits
 
     @torch.no_grad()
-    def generate_graph(self, prompt: torch.Tensor, steps: int, tau_mode="median") -> Dict:
+    def generate_graph(self, prompt: torch.Tensor, steps: int, tau_mode="median", dense: bool = False) -> Dict:
         """Greedy decoding with each decode step replayed from one captured CUDA graph.
 
         Prefill and the first step run eagerly (the first step calibrates each
         layer's tau); the step is then captured once and replayed ``steps - 1``
         times, with lengths and tokens kept on the device (no host sync per token).
         Returns the per-step device time (CUDA events around the replays).
+        ``dense=True`` times the dense arm: the same step with flashinfer
+        decoding over the prompt's tokens (a fixed window) in place of the
+        fused kernel; its tokens are not a faithful greedy continuation.
         """
         self.length = 0
         self.tau = [None] * self.s.layers
         logits = self.prefill(prompt)
         tok = logits.argmax(-1)
-        first = self.step(tok, tau_mode)            # eager: sets self.tau
+        first = self.step(tok, "flash" if dense else tau_mode)   # eager: sets self.tau
+        window = prompt.shape[0] if dense else None
         tok_d = first.argmax(-1).reshape(1).clone()
         npos = torch.full((1,), self.length, dtype=torch.long, device=self.dev)
         st = torch.cuda.Stream()
@@ -272,12 +300,12 @@ class GatedLlama:
         with torch.cuda.stream(st):
             # a warm-up step outside the capture (workspaces, tensor maps), undone afterwards
             t0, n0 = tok_d.clone(), npos.clone()
-            self._step_dev(tok_d, npos)
+            self._step_dev(tok_d, npos, window)
             tok_d.copy_(t0)
             npos.copy_(n0)
             torch.cuda.synchronize()
             with torch.cuda.graph(g, stream=st):
-                self._step_dev(tok_d, npos)
+                self._step_dev(tok_d, npos, window)
         torch.cuda.current_stream().wait_stream(st)
         toks = [int(tok), int(tok_d)]
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
