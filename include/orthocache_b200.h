@@ -293,7 +293,10 @@ int oc_rope_cache_append(const void* qkv, int heads, int kv_heads, int head_dim,
  * down to 64, merged by log-sum-exp with the state (m in log2 units, l,
  * unnormalised acc (heads, head_dim), float32) that the fused kernel returned
  * for tokens [0, full) (oc_fused_attention_v3_shard).  scale_log2 =
- * log2(e) / sqrt(head_dim).  out (heads, head_dim) in dtype. */
+ * log2(e) / sqrt(head_dim).  out (heads, head_dim) in dtype.  The launch is a
+ * programmatic dependent of the kernel before it on the stream (the one that
+ * wrote m / l / acc): q and the caches are read before it waits, so they must
+ * be complete by the time that kernel starts. */
 int oc_tail_merge(const void* q, int heads, int kv_heads, int head_dim, const void* k_cache, const void* v_cache,
                   int64_t cache_token_stride, int64_t max_len, const int64_t* pos, const float* m, const float* l,
                   const float* acc, float scale_log2, void* out, int dtype, void* stream);

@@ -459,9 +459,10 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   mbar_init_fence();
   __syncwarp();
 
-  // LIST mode: the lists come from the gate kernel, launched just before as
-  // this grid's programmatic predecessor; everything above overlapped it
-  if (p.list_count != nullptr) asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Every launch is a programmatic dependent of the kernel before it on the
+  // stream (in LIST mode the gate kernel that wrote the lists): everything
+  // above overlapped that kernel's tail; nothing above reads global memory
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // ---- tiles per unit, prefix in shared memory.  Without per-sequence
   // lengths or tile lists every unit has num_tiles tiles: each warp writes
   // the whole prefix itself (every warp writes the same values), so no block
@@ -1489,6 +1490,9 @@ __global__ void __launch_bounds__(32 * kMergeWarps) merge_kernel(const DecodePar
 #ifdef OC_TRACE
   const unsigned long long tr_m0 = oc_clock();
 #endif
+  // the next kernel on the stream may be scheduled now; it waits for this grid
+  // (griddepcontrol.wait) before it reads what this grid writes
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 #ifdef OC_TRACE
   if (p.trace != nullptr && threadIdx.x == 0) {
@@ -1625,7 +1629,7 @@ cudaError_t launch_decode(const DecodeParams& p, const CUtensorMap& tk, const CU
   da[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   da[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = da;
-  cfg.numAttrs = p.list_count != nullptr ? 1 : 0;  // LIST mode follows its gate kernel
+  cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p, tk, tv);
   if (e != cudaSuccess || !ATTN) return e;
   // merge of the units shared by several teams: a programmatic dependent launch

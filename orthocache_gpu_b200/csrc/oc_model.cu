@@ -147,6 +147,10 @@ __global__ void tail_merge_kernel(const T* q, int group, int hd, const T* k_cach
   const float p = exp2f(lg - mt);
   pt[t] = p;
   const float lt = block_sum(p, red);  // its barriers also publish pt
+  // the state of the whole tiles comes from the kernel before this one (a
+  // programmatic dependent launch: everything above overlapped it)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const float m0 = m_in[h], M = fmaxf(m0, mt);
   const float a = exp2f(m0 - M), b = exp2f(mt - M);
   const float L = fmaf(l_in[h], a, lt * b);
@@ -214,17 +218,27 @@ extern "C" int oc_tail_merge(const void* q, int heads, int kv_heads, int head_di
     return OC_ERR_INVALID;
   auto st = static_cast<cudaStream_t>(stream);
   const int group = heads / kv_heads;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)heads);
+  cfg.blockDim = dim3(64);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   if (dtype == OC_BF16)
-    tail_merge_kernel<__nv_bfloat16><<<(unsigned)heads, 64, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(q), group, head_dim, static_cast<const __nv_bfloat16*>(k_cache),
-        static_cast<const __nv_bfloat16*>(v_cache), cache_token_stride, max_len, pos, m, l, acc, scale_log2,
-        static_cast<__nv_bfloat16*>(out));
+    e = cudaLaunchKernelEx(&cfg, tail_merge_kernel<__nv_bfloat16>, static_cast<const __nv_bfloat16*>(q), group,
+                           head_dim, static_cast<const __nv_bfloat16*>(k_cache),
+                           static_cast<const __nv_bfloat16*>(v_cache), cache_token_stride, max_len, pos, m, l, acc,
+                           scale_log2, static_cast<__nv_bfloat16*>(out));
   else if (dtype == OC_F16)
-    tail_merge_kernel<__half><<<(unsigned)heads, 64, 0, st>>>(
-        static_cast<const __half*>(q), group, head_dim, static_cast<const __half*>(k_cache),
-        static_cast<const __half*>(v_cache), cache_token_stride, max_len, pos, m, l, acc, scale_log2,
-        static_cast<__half*>(out));
+    e = cudaLaunchKernelEx(&cfg, tail_merge_kernel<__half>, static_cast<const __half*>(q), group, head_dim,
+                           static_cast<const __half*>(k_cache), static_cast<const __half*>(v_cache),
+                           cache_token_stride, max_len, pos, m, l, acc, scale_log2, static_cast<__half*>(out));
   else
     return OC_ERR_UNSUPPORTED;
+  if (e != cudaSuccess) return OC_ERR_CUDA;
   return finish();
 }
