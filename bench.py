@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only: no sweep, e2e or CPU baseline (profiling target)")
-    ap.add_argument("--workload", default="v2", choices=["v2", "v3", "paged", "cached"],
+    ap.add_argument("--workload", default="v2", choices=["v2", "v3", "paged", "cached", "model"],
                     help="with --quick: the configuration to time (profiling targets of the other kernels)")
     ap.add_argument("--num-seqs", type=int, default=16, help="with --quick: sequences of the v3/paged/cached case")
     ap.add_argument("--e2e-steps", type=int, default=10)
@@ -262,6 +262,19 @@ def quick_workload(a, dev):
     import orthocache_gpu_b200 as oc
     g = torch.Generator(device=dev)
     g.manual_seed(3)
+    if a.workload == "model":
+        # the TinyLlama-shaped decode step (config 5b); the third replay of the captured
+        # step runs between cudaProfilerStart / Stop (ncu --profile-from-start off)
+        from orthocache_gpu_b200.model import GatedLlama, LlamaShape
+        m = GatedLlama(LlamaShape(), max_len=16384 + 320, device=dev, seed=5)
+        prompt = torch.randint(0, 32000, (16384,), generator=g, device=dev)
+        steps = max(4, min(a.steps, 256))
+        r = m.generate_graph(prompt, steps, tau_mode="median", profile_replay=2)
+        d = m.generate_graph(prompt, steps, dense=True)
+        print(json.dumps({"workload": "model", "steps": steps, "fused_graph_ms_per_token": round(r["ms_per_token"], 4),
+                          "dense_flashinfer_graph_ms_per_token": round(d["ms_per_token"], 4),
+                          "weight_bytes": m.weight_bytes()}))
+        return
     KVH, G, HD, TAU = 8, 4, 128, 150.0
     if a.workload in ("v3", "cached"):
         B, S = a.num_seqs, 32768

@@ -6,11 +6,13 @@
 // layer; each is HBM-bound, so the kernel's job is to stream W's rows with
 // long contiguous reads and enough bytes in flight on every SM.
 //
-//   Persistent grid (two CTAs of 16 warps per SM at most); each warp takes
+//   Persistent grid (one wave of resident CTAs of 16 warps); each warp takes
 //   PAIRS of output rows in turn and reads both rows in 2048-column pieces:
 //   lane l loads 16 bytes at columns 8 (l + 32 i), i < 8, of each row (16
 //   loads of 16 bytes in flight per lane, 4 KB contiguous per row and piece),
-//   then a butterfly reduction gives the two dot products.  The pair is
+//   then a butterfly reduction gives the two dot products (with few pairs
+//   and K > 2048, two or four warps of a CTA share a pair, one piece each in
+//   turn, and add their sums through shared memory).  The pair is
 //   what the epilogues need together:
 //     PLAIN     rows (2p, 2p+1)          out[n] = round(sum_n)
 //     SILU_MUL  rows (2j, 2j+1) = (a_j, b_j), W's rows interleaved
@@ -78,13 +80,16 @@ template <typename T, int EPI>
 __global__ void __launch_bounds__(32 * kWarps) gemv_kernel(const T* __restrict__ x, const T* __restrict__ y,
                                                           const T* __restrict__ norm_w, float eps,
                                                           T* __restrict__ x_out, const T* __restrict__ W,
-                                                          int64_t ldw, int K, int N, T* __restrict__ out,
-                                                          RopeArgs ra) {
+                                                          int64_t ldw, int K, int N, int S,
+                                                          T* __restrict__ out, RopeArgs ra) {
   __shared__ __align__(16) float hs[kMaxK];
   __shared__ float wsum[kWarps];
+  __shared__ float2 part[kWarps];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int npairs = N / 2;
-  const int64_t gw = (int64_t)blockIdx.x * kWarps + warp, nw = (int64_t)gridDim.x * kWarps;
+  // S warps share a pair (S = 1, 2 or 4): warp `sub` of the group reads pieces sub, sub + S, ...
+  const int sub = warp % S, slot = warp / S, slots = kWarps / S;
+  const int64_t gw = (int64_t)blockIdx.x * slots + slot, nw = (int64_t)gridDim.x * slots;
 
   // rows of pair p
   auto rows = [&](int p, int& r0, int& r1) {
@@ -116,7 +121,8 @@ __global__ void __launch_bounds__(32 * kWarps) gemv_kernel(const T* __restrict__
   };
   // the first pair's first piece goes out before the activations are read
   int p = (int)gw;
-  if (p < npairs) load_piece(p, 0);
+  const int kfirst = sub * kPiece;
+  if (p < npairs && kfirst < K) load_piece(p, kfirst);
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -157,8 +163,8 @@ __global__ void __launch_bounds__(32 * kWarps) gemv_kernel(const T* __restrict__
 
   for (; p < npairs; p += (int)nw) {
     float s0 = 0.f, s1 = 0.f;
-    for (int k0 = 0; k0 < K; k0 += kPiece) {
-      if (k0 > 0) load_piece(p, k0);
+    for (int k0 = kfirst; k0 < K; k0 += S * kPiece) {
+      if (k0 > kfirst) load_piece(p, k0);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int k = k0 + 8 * (lane + 32 * i);
@@ -176,11 +182,25 @@ __global__ void __launch_bounds__(32 * kWarps) gemv_kernel(const T* __restrict__
         }
       }
     }
-    if (p + nw < npairs) load_piece((int)(p + nw), 0);  // next pair's first piece before the reduction
+    if (p + nw < npairs && kfirst < K) load_piece((int)(p + nw), kfirst);  // next pair, before the reduction
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       s0 += __shfl_xor_sync(0xffffffffu, s0, o);
       s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    }
+    if (S > 1) {  // the group's partial sums, added in piece order by its first warp
+      if (lane == 0) part[warp] = make_float2(s0, s1);
+      asm volatile("bar.sync %0, %1;" ::"r"(slot + 1), "r"(32 * S) : "memory");
+      if (sub == 0) {
+        s0 = 0.f;
+        s1 = 0.f;
+        for (int j = 0; j < S; ++j) {
+          s0 += part[warp + j].x;
+          s1 += part[warp + j].y;
+        }
+      }
+      asm volatile("bar.sync %0, %1;" ::"r"(slot + 1), "r"(32 * S) : "memory");
+      if (sub != 0) continue;
     }
     if (lane != 0) continue;
     int r0, r1;
@@ -235,8 +255,24 @@ template <typename T, int EPI>
 int launch(const void* x, const void* y, const void* norm_w, float eps, void* x_out, const void* W, int64_t ldw,
            int64_t K, int64_t N, void* out, const RopeArgs& ra, cudaStream_t st) {
   const int64_t npairs = N / 2;
-  int64_t grid = (npairs + kWarps - 1) / kWarps;
-  if (grid > 2 * (int64_t)sms()) grid = 2 * (int64_t)sms();
+  // persistent: every CTA resident at once (one wave)
+  static int per_sm[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int occ = dev >= 0 && dev < 64 ? per_sm[dev] : 0;
+  if (occ == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_kernel<T, EPI>, 32 * kWarps, 0) != cudaSuccess ||
+        occ < 1)
+      occ = 1;
+    if (dev >= 0 && dev < 64) per_sm[dev] = occ;
+  }
+  // warps per pair: enough pair tasks for every resident warp, at most one per 2048-column piece
+  const int64_t warps = (int64_t)occ * sms() * kWarps, pieces = (K + kPiece - 1) / kPiece;
+  int S = 1;
+  while (S < 4 && 2 * S <= pieces && npairs * S < warps) S *= 2;
+  const int64_t slots = kWarps / S;
+  int64_t grid = (npairs + slots - 1) / slots;
+  if (grid > (int64_t)occ * sms()) grid = (int64_t)occ * sms();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(32 * kWarps);
@@ -248,7 +284,7 @@ int launch(const void* x, const void* y, const void* norm_w, float eps, void* x_
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, gemv_kernel<T, EPI>, static_cast<const T*>(x), static_cast<const T*>(y),
                          static_cast<const T*>(norm_w), eps, static_cast<T*>(x_out), static_cast<const T*>(W), ldw,
-                         (int)K, (int)N, static_cast<T*>(out), ra) != cudaSuccess)
+                         (int)K, (int)N, S, static_cast<T*>(out), ra) != cudaSuccess)
     return OC_ERR_CUDA;
   return OC_OK;
 }

@@ -275,7 +275,8 @@ class GatedLlama:
         return logits
 
     @torch.no_grad()
-    def generate_graph(self, prompt: torch.Tensor, steps: int, tau_mode="median", dense: bool = False) -> Dict:
+    def generate_graph(self, prompt: torch.Tensor, steps: int, tau_mode="median", dense: bool = False,
+                       profile_replay: Optional[int] = None) -> Dict:
         """Greedy decoding with each decode step replayed from one captured CUDA graph.
 
         Prefill and the first step run eagerly (the first step calibrates each
@@ -311,8 +312,12 @@ class GatedLlama:
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         hist = []
-        for _ in range(steps - 1):
+        for i in range(steps - 1):
+            if i == profile_replay:
+                torch.cuda.cudart().cudaProfilerStart()
             g.replay()
+            if i == profile_replay:
+                torch.cuda.cudart().cudaProfilerStop()
             hist.append(tok_d.clone())
         b.record()
         torch.cuda.synchronize()
