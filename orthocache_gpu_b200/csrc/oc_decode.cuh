@@ -460,9 +460,13 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
   __syncwarp();
 
   // Every launch is a programmatic dependent of the kernel before it on the
-  // stream (in LIST mode the gate kernel that wrote the lists): everything
-  // above overlapped that kernel's tail; nothing above reads global memory
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // stream (in LIST mode the gate kernel that wrote the lists): the set-up
+  // that reads no global memory overlaps that kernel's tail.  Without
+  // per-sequence lengths or tile lists that is everything up to the first
+  // read of q (the tile prefix and the team's range come from the
+  // parameters); otherwise the prefix reads them, so the wait comes first.
+  const bool late_wait = p.seq_lens == nullptr && p.list_count == nullptr;
+  if (!late_wait) asm volatile("griddepcontrol.wait;" ::: "memory");
   // ---- tiles per unit, prefix in shared memory.  Without per-sequence
   // lengths or tile lists every unit has num_tiles tiles: each warp writes
   // the whole prefix itself (every warp writes the same values), so no block
@@ -724,6 +728,7 @@ __global__ void __launch_bounds__(Cfg<KT, VT, HD, GC, ATTN, NSLOT, TC>::NT, 1)
 #ifdef OC_TRACE
   tr_b = oc_clock();
 #endif
+  if (late_wait) asm volatile("griddepcontrol.wait;" ::: "memory");
   if (fb > fa) enter_unit(u_first, fa);
 #ifdef OC_TRACE
   unsigned long long tr_c = oc_clock(), tr_d = 0;

@@ -213,7 +213,7 @@ class GatedLlama:
         """One decode step from device state: tok (1,) next token, npos (1,) cache length;
         both are updated in place (argmax token, length + 1).
 
-        Eight launches per layer: the q|k|v GEMV with the residual add + RMSNorm
+        Seven launches per layer: the q|k|v GEMV with the residual add + RMSNorm
         in its prologue and rotary embedding + cache append in its epilogue;
         the fused decode attention over whole tiles (+ its merge) and the
         ragged-tail merge; the output projection; the MLP input GEMV (residual
