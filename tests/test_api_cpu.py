@@ -57,6 +57,15 @@ def test_c_abi_rejects_bad_arguments_without_a_gpu():
     addr = (ctypes.addressof(buf) + 15) & ~15
     st = ctypes.c_uint32(0)
     assert l.oc_fwht_eviction(addr, 1, 64, 100, 100, 5.0, addr, None, ctypes.addressof(st), None) == 2
+    # model-step GEMV: null input, K not a multiple of 8, odd N, K beyond the prologue limit, odd head_dim
+    assert l.oc_gemv(None, None, None, 1e-5, None, addr, 64, 64, 64, addr, 0, 2, None) == 1
+    assert l.oc_gemv(addr, None, None, 1e-5, None, addr, 64, 60, 64, addr, 0, 2, None) == 1
+    assert l.oc_gemv(addr, None, None, 1e-5, None, addr, 64, 64, 63, addr, 0, 2, None) == 1
+    assert l.oc_gemv(addr, None, addr, 1e-5, None, addr, 16384, 16384, 64, addr, 0, 2, None) == 1
+    assert l.oc_gemv(addr, None, None, 1e-5, None, addr, 64, 64, 64, addr, 7, 2, None) == 1   # epilogue
+    assert l.oc_gemv(addr, None, addr, 1e-5, addr, addr, 64, 64, 64, addr, 0, 2, None) == 1  # x_out aliases x
+    assert l.oc_gemv_qkv_rope(addr, None, addr, 1e-5, None, addr, 64, 64, 8, 2, 63, addr, addr, addr, addr, addr,
+                              addr, 256, 2, None) == 1
 
 
 def _t(*shape):
