@@ -103,12 +103,12 @@ def _gemv_ref(x, y, norm_w, W, eps=1e-5):
 @pytest.mark.parametrize("K,N,norm,epi", [(2048, 3072, True, 0), (2048, 2048, False, 0), (5632, 2048, False, 0),
                                           (2048, 11264, True, 1), (2048, 32000, True, 0), (96, 264, False, 0),
                                           (4104, 6, True, 1)])
-def test_gemv_matches_torch(K, N, norm, epi):
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_gemv_matches_torch(K, N, norm, epi, dt):
     from orthocache_gpu_b200 import _lib
     lib = _lib.load()
     g = torch.Generator(device="cuda")
     g.manual_seed(K + N)
-    dt = torch.bfloat16
     x = torch.randn(1, K, device="cuda", generator=g).to(dt)
     y = torch.randn(1, K, device="cuda", generator=g).to(dt) if norm else None
     nw = (1 + 0.1 * torch.randn(K, device="cuda", generator=g)).to(dt) if norm else None
